@@ -1,0 +1,135 @@
+/*
+ * fmm_sm100.h -- C ABI of libfmm_sm100.so, the B200 (sm_100a) kernels behind
+ * the rdna3_fastmm operator surface.
+ *
+ * The reference (chelokot/rdna3-fastmm) has no C layer: its plans launch
+ * generated Triton kernels and torch.bmm directly from Python.  Each entry
+ * point below replaces one of those launches; the citation names the
+ * reference call it stands in for (paths are inside the reference project).
+ *
+ * Conventions for every entry point:
+ *   - all pointers are caller-owned device pointers; nothing is allocated,
+ *     freed, retained or synchronised (work is queued on `stream`);
+ *   - BF16 tensors are row-major with the given leading dimension in
+ *     elements; FP16 planes are stacked [rank][rows][pitch] with
+ *     pitch = round_up(cols, 8) elements (fmm_plan_dims), which keeps every
+ *     row 16-byte aligned for TMA; plane buffers must be 16-byte aligned;
+ *   - the return value is FMM_OK or an FMM_ERR_* code; fmm_last_error_string
+ *     describes the last failure of the calling thread.
+ *
+ * Transformed planes use the layout [rank][rows][cols]:
+ *   left  (activations)  L[r][bm][ldk]   -- as the reference's L[r][bm][bk]
+ *   right (weight)       Rt[r][bn][ldk]  -- the TRANSPOSE of the reference's
+ *                                           Rw[r][bk][bn], i.e. K-major, the
+ *                                           operand layout tcgen05 reads
+ *   products             P[r][bm][ldp]   -- as the reference's P[r][bm][bn]
+ */
+#ifndef FMM_SM100_H
+#define FMM_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* fmm_stream_t; /* == cudaStream_t */
+
+#define FMM_OK 0
+#define FMM_ERR_INVALID_ARGUMENT 1
+#define FMM_ERR_MISALIGNED 2
+#define FMM_ERR_UNSUPPORTED 3
+#define FMM_ERR_CUDA 4
+#define FMM_ERR_DEVICE_TIMEOUT 5
+#define FMM_ERR_TOO_LARGE 6
+
+/* scheme ids: the rank of the block scheme */
+#define FMM_SCHEME_RANK7 7   /* <2,2,2> rank 7 (Strassen-Winograd form)  */
+#define FMM_SCHEME_RANK48 48 /* <4,4,4> rank 48 dyadic-rational SLP        */
+#define FMM_SCHEME_RANK49 49 /* <4,4,4> rank 49 (rank 7 (x) rank 7)        */
+
+/* bits of the device status word */
+#define FMM_STATUS_TIMEOUT 1u
+
+/* fmm_linear flags */
+#define FMM_LINEAR_PREPACKED 1u /* `weight_planes` already hold the packed Rt */
+
+typedef struct fmm_dims {
+  int64_t scheme_size; /* s                      */
+  int64_t rank;        /* R                      */
+  int64_t bm, bk, bn;  /* ceil(M/s), ceil(K/s), ceil(N/s) */
+  int64_t ldk;         /* pitch of L and Rt rows = round_up(bk, 8) */
+  int64_t ldp;         /* pitch of P rows        = round_up(bn, 8) */
+  int64_t left_elements;    /* R*bm*ldk */
+  int64_t right_elements;   /* R*bn*ldk */
+  int64_t product_elements; /* R*bm*ldp */
+} fmm_dims;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int fmm_version(void);
+
+/* Text of the calling thread's last error ("" if none). */
+const char* fmm_last_error_string(void);
+
+/* Block dimensions and plane sizes for an M x K x N linear.
+ * Replaces MatrixShape.from_dimensions (src/rdna3_fastmm/runtime.py:56-89). */
+int fmm_plan_dims(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* out);
+
+/* A[M,K] (BF16, lda) -> L[R][bm][ldk] (FP16).
+ * Replaces left_transform_kernel (src/rdna3_fastmm/runtime.py:597-615;
+ * src/rdna3_fastmm/generated/rank7_2x2x2.py:9-62 and the rank-48/49 twins). */
+int fmm_transform_a(int scheme, const void* A, int64_t M, int64_t K, int64_t lda, void* L,
+                    fmm_stream_t stream);
+
+/* weight[N,K] (BF16, ldw) -> Rt[R][bn][ldk] (FP16), the transform of
+ * B = weight^T stored K-major.  Used per call (dynamic) and once (prepack).
+ * Replaces right_transform_weight_kernel (src/rdna3_fastmm/runtime.py:637-655;
+ * src/rdna3_fastmm/generated/rank7_2x2x2.py:121-204 and twins). */
+int fmm_transform_w(int scheme, const void* W, int64_t N, int64_t K, int64_t ldw, void* Rt,
+                    fmm_stream_t stream);
+
+/* P[r] = L[r] * Rt[r]^T for r < rank: FP16 operands, FP32 accumulation in
+ * tensor memory, FP16 products.  tcgen05 + TMA, persistent over 148 SMs.
+ * Replaces torch.bmm(L, Rw, out=P) (src/rdna3_fastmm/runtime.py:728-732). */
+int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
+                  void* P, fmm_stream_t stream);
+
+/* P[R][bm][ldp] (FP16) -> C[M,N] (BF16, ldc) with optional bias[N] (BF16,
+ * may be NULL): FP32 recombination, bias added last, round to nearest even.
+ * Replaces output_transform_kernel / output_transform_bias_kernel
+ * (src/rdna3_fastmm/runtime.py:657-698). */
+int fmm_reconstruct(int scheme, const void* P, int64_t M, int64_t N, const void* bias, void* C,
+                    int64_t ldc, fmm_stream_t stream);
+
+/* The whole F.linear: C = A * weight^T (+ bias) through the scheme, using the
+ * caller's planes (L, Rt, P sized by fmm_plan_dims).  With
+ * FMM_LINEAR_PREPACKED, `weight` is ignored (may be NULL) and `Rt` holds
+ * planes produced earlier by fmm_transform_w.
+ * Replaces _LinearPlan.run_linear / run_linear_packed
+ * (src/rdna3_fastmm/runtime.py:700-777). */
+int fmm_linear(int scheme, const void* A, const void* W, const void* bias, void* C, int64_t M,
+               int64_t K, int64_t N, void* L, void* Rt, void* P, unsigned int flags,
+               fmm_stream_t stream);
+
+/* Upper bound, in nanoseconds, of every device-side wait (default 2 s).  A
+ * wait that runs out records FMM_STATUS_TIMEOUT and unwinds the kernel.  No
+ * counterpart in the reference (it has no device-side waits). */
+int fmm_set_wait_timeout_ns(uint64_t timeout_ns);
+
+/* Synchronise `device` and read its status word; clear it when `reset`.
+ * `site` (may be NULL) receives where the first timeout happened.  No
+ * counterpart in the reference. */
+int fmm_device_status(int device, uint32_t* status, uint32_t* site, int reset);
+
+/* Test hook for the bounded waits: launches one CTA that waits, with
+ * `timeout_ns`, on an mbarrier nothing arrives on.  The wait must run out and
+ * the kernel must return; the caller then reads FMM_STATUS_TIMEOUT with
+ * fmm_device_status.  No counterpart in the reference. */
+int fmm_test_bounded_wait(uint64_t timeout_ns, fmm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FMM_SM100_H */

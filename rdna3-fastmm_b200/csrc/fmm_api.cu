@@ -1,0 +1,404 @@
+// C ABI of libfmm_sm100.so: argument checking, launch geometry, TMA tensor
+// maps, and the per-scheme dispatch of the generated transforms.
+//
+// Nothing here allocates device memory or synchronises the stream (except
+// fmm_device_status, whose job is to synchronise and read the status word).
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fmm_common.cuh"
+#include "transforms.cuh"
+#include "generated/fmm_schemes.cuh"
+#include "leaf_gemm.cuh"
+
+namespace fmm {
+
+namespace {
+
+thread_local std::string t_last_error;
+uint64_t g_timeout_ns = 2000000000ull;  // 2 s per wait
+
+int fail(int code, const std::string& what) {
+  t_last_error = what;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(FMM_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
+}
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t round_up(int64_t a, int64_t b) { return ceil_div(a, b) * b; }
+
+int scheme_size(int scheme) {
+  switch (scheme) {
+    case FMM_SCHEME_RANK7: return 2;
+    case FMM_SCHEME_RANK48: return 4;
+    case FMM_SCHEME_RANK49: return 4;
+    default: return 0;
+  }
+}
+
+int dims_for(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* d) {
+  const int s = scheme_size(scheme);
+  if (s == 0) return fail(FMM_ERR_UNSUPPORTED, "unknown scheme id " + std::to_string(scheme));
+  if (M < 1 || K < 1 || N < 1) return fail(FMM_ERR_INVALID_ARGUMENT, "matrix dimensions must be positive");
+  d->scheme_size = s;
+  d->rank = scheme;
+  d->bm = ceil_div(M, s);
+  d->bk = ceil_div(K, s);
+  d->bn = ceil_div(N, s);
+  d->ldk = round_up(d->bk, 8);
+  d->ldp = round_up(d->bn, 8);
+  d->left_elements = d->rank * d->bm * d->ldk;
+  d->right_elements = d->rank * d->bn * d->ldk;
+  d->product_elements = d->rank * d->bm * d->ldp;
+  // 32-bit per-plane vector indices in the streaming kernels; TMA coordinates
+  if (d->bm * d->ldk > (int64_t(1) << 31) || d->bn * d->ldk > (int64_t(1) << 31) ||
+      d->bm * d->ldp > (int64_t(1) << 31) || d->bm > (int64_t(1) << 30) ||
+      d->bn > (int64_t(1) << 30))
+    return fail(FMM_ERR_TOO_LARGE, "transform planes exceed 2^31 elements");
+  return FMM_OK;
+}
+
+struct DeviceInfo {
+  int sm_count = 0;
+  bool gemm_configured = false;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_device_mutex;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_device_mutex);
+  DeviceInfo& info = g_devices[dev];
+  if (info.sm_count == 0) {
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    if (major != 10 || minor != 0)
+      return fail(FMM_ERR_UNSUPPORTED, "libfmm_sm100 needs an sm_100 (B200) device; found sm_" +
+                                           std::to_string(major) + std::to_string(minor));
+    info.sm_count = sms;
+  }
+  *out = &info;
+  return FMM_OK;
+}
+
+// ------------------------------------------------------------------ dispatch
+template <int SCHEME>
+struct SchemeTraits;
+template <>
+struct SchemeTraits<FMM_SCHEME_RANK7> {
+  using Left = gen::Rank7Left;
+  using Right = gen::Rank7Right;
+  using Output = gen::Rank7Output;
+  static constexpr int S = 2;
+  static constexpr int VEC = 8;
+};
+template <>
+struct SchemeTraits<FMM_SCHEME_RANK48> {
+  using Left = gen::Rank48Left;
+  using Right = gen::Rank48Right;
+  using Output = gen::Rank48Output;
+  static constexpr int S = 4;
+  static constexpr int VEC = 4;
+};
+template <>
+struct SchemeTraits<FMM_SCHEME_RANK49> {
+  using Left = gen::Rank49Left;
+  using Right = gen::Rank49Right;
+  using Output = gen::Rank49Output;
+  static constexpr int S = 4;
+  static constexpr int VEC = 4;
+};
+
+int streaming_grid(const DeviceInfo* info, int64_t work_items) {
+  const int64_t blocks = ceil_div(work_items, 256);
+  const int64_t cap = int64_t(info->sm_count) * 16;
+  return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+template <int SCHEME, bool kWeight>
+int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t ld, void* dst,
+                           int64_t brows, int64_t bcols, int64_t ldd, cudaStream_t stream) {
+  using T = SchemeTraits<SCHEME>;
+  DeviceInfo* info = nullptr;
+  if (int rc = device_info(&info)) return rc;
+  const bool vec = (bcols % T::VEC == 0) && (ld % T::VEC == 0) && aligned(src, 2 * T::VEC);
+  const int64_t items = brows * (ldd / T::VEC);
+  using Prog = typename std::conditional<kWeight, typename T::Right, typename T::Left>::type;
+  block_transform_kernel<Prog, T::S, T::VEC, kWeight>
+      <<<streaming_grid(info, items), 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(src), rows, cols, ld, static_cast<__half*>(dst), brows,
+          bcols, ldd, vec ? 1 : 0);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, kWeight ? "weight transform launch" : "left transform launch");
+  return FMM_OK;
+}
+
+template <int SCHEME>
+int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
+                       void* C, int64_t ldc, cudaStream_t stream) {
+  using T = SchemeTraits<SCHEME>;
+  DeviceInfo* info = nullptr;
+  if (int rc = device_info(&info)) return rc;
+  const bool vec = (d.bn % T::VEC == 0) && (ldc % T::VEC == 0) && aligned(C, 2 * T::VEC);
+  const int64_t items = d.bm * ceil_div(d.bn, T::VEC);
+  reconstruct_kernel<typename T::Output, T::S, T::VEC>
+      <<<streaming_grid(info, items), 256, 0, stream>>>(
+          static_cast<const __half*>(P), d.bm, d.bn, d.ldp,
+          static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(C), M, N, ldc,
+          vec ? 1 : 0);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
+  return FMM_OK;
+}
+
+// ------------------------------------------------------------------ TMA maps
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr) return fail(FMM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  *out = g_encode;
+  return FMM_OK;
+}
+
+// Stacked FP16 planes [batch][rows][pitch] as a 3-D map over (k, row, batch);
+// box = 64 K-elements (128 B, swizzled) x box_rows rows x 1 plane.
+int plane_map(CUtensorMap* map, const void* base, int64_t k, int64_t rows, int64_t pitch,
+              int64_t batch, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (int rc = tensor_map_encoder(&encode)) return rc;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch * 2),
+                           static_cast<cuuint64_t>(pitch * 2 * rows)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kGemmBK), box_rows, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
+                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return FMM_OK;
+}
+
+using GemmCfg = LeafGemmConfig<256, 4>;
+
+int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
+                     void* P, cudaStream_t stream) {
+  if (rank < 1 || bm < 1 || bn < 1 || bk < 1)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "leaf GEMM dimensions must be positive");
+  if (!aligned(L, 16) || !aligned(Rt, 16) || !aligned(P, 16))
+    return fail(FMM_ERR_MISALIGNED, "leaf GEMM planes must be 16-byte aligned");
+  DeviceInfo* info = nullptr;
+  if (int rc = device_info(&info)) return rc;
+  const int64_t ldk = round_up(bk, 8), ldp = round_up(bn, 8);
+  CUtensorMap map_l, map_r;
+  if (int rc = plane_map(&map_l, L, bk, bm, ldk, rank, kGemmBM)) return rc;
+  if (int rc = plane_map(&map_r, Rt, bk, bn, ldk, rank, GemmCfg::kBN)) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (!info->gemm_configured) {
+      cudaError_t e = cudaFuncSetAttribute(leaf_gemm_kernel<GemmCfg>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(GemmCfg::kSmemBytes));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(leaf GEMM)");
+      info->gemm_configured = true;
+    }
+  }
+  LeafGemmParams prm;
+  prm.bm = bm;
+  prm.bn = bn;
+  prm.bk = bk;
+  prm.ldp = ldp;
+  prm.rank = rank;
+  prm.tiles_m = static_cast<int32_t>(ceil_div(bm, kGemmBM));
+  prm.tiles_n = static_cast<int32_t>(ceil_div(bn, GemmCfg::kBN));
+  prm.group_m = 16;
+  prm.P = static_cast<__half*>(P);
+  prm.timeout_ns = g_timeout_ns;
+  const int64_t tiles = int64_t(rank) * prm.tiles_m * prm.tiles_n;
+  if (tiles > (int64_t(1) << 30)) return fail(FMM_ERR_TOO_LARGE, "too many GEMM tiles");
+  const int grid = static_cast<int>(tiles < info->sm_count ? tiles : info->sm_count);
+  leaf_gemm_kernel<GemmCfg><<<grid, kGemmThreads, GemmCfg::kSmemBytes, stream>>>(map_l, map_r, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM launch");
+  return FMM_OK;
+}
+
+__global__ void bounded_wait_probe_kernel(uint64_t timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // nothing ever arrives: the wait must give up after timeout_ns
+    mbar_wait_bounded(smem_u32(&bar), 0, &abort_flag, timeout_ns, 7);
+  }
+  __syncthreads();
+}
+
+}  // namespace
+}  // namespace fmm
+
+using namespace fmm;
+
+extern "C" {
+
+int fmm_version(void) { return 100; }
+
+const char* fmm_last_error_string(void) { return t_last_error.c_str(); }
+
+int fmm_plan_dims(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* out) {
+  if (out == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null output");
+  return dims_for(scheme, M, K, N, out);
+}
+
+int fmm_transform_a(int scheme, const void* A, int64_t M, int64_t K, int64_t lda, void* L,
+                    fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, M, K, 1, &d)) return rc;
+  if (A == nullptr || L == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  if (lda < K) return fail(FMM_ERR_INVALID_ARGUMENT, "lda < K");
+  if (!aligned(L, 16)) return fail(FMM_ERR_MISALIGNED, "L must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (scheme) {
+    case FMM_SCHEME_RANK7:
+      return launch_input_transform<FMM_SCHEME_RANK7, false>(A, M, K, lda, L, d.bm, d.bk, d.ldk, s);
+    case FMM_SCHEME_RANK48:
+      return launch_input_transform<FMM_SCHEME_RANK48, false>(A, M, K, lda, L, d.bm, d.bk, d.ldk, s);
+    default:
+      return launch_input_transform<FMM_SCHEME_RANK49, false>(A, M, K, lda, L, d.bm, d.bk, d.ldk, s);
+  }
+}
+
+int fmm_transform_w(int scheme, const void* W, int64_t N, int64_t K, int64_t ldw, void* Rt,
+                    fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, 1, K, N, &d)) return rc;
+  if (W == nullptr || Rt == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldw < K) return fail(FMM_ERR_INVALID_ARGUMENT, "ldw < K");
+  if (!aligned(Rt, 16)) return fail(FMM_ERR_MISALIGNED, "Rt must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (scheme) {
+    case FMM_SCHEME_RANK7:
+      return launch_input_transform<FMM_SCHEME_RANK7, true>(W, N, K, ldw, Rt, d.bn, d.bk, d.ldk, s);
+    case FMM_SCHEME_RANK48:
+      return launch_input_transform<FMM_SCHEME_RANK48, true>(W, N, K, ldw, Rt, d.bn, d.bk, d.ldk, s);
+    default:
+      return launch_input_transform<FMM_SCHEME_RANK49, true>(W, N, K, ldw, Rt, d.bn, d.bk, d.ldk, s);
+  }
+}
+
+int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
+                  void* P, fmm_stream_t stream) {
+  if (L == nullptr || Rt == nullptr || P == nullptr)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  return launch_leaf_gemm(rank, L, Rt, bm, bn, bk, P, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fmm_reconstruct(int scheme, const void* P, int64_t M, int64_t N, const void* bias, void* C,
+                    int64_t ldc, fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, M, 1, N, &d)) return rc;
+  if (P == nullptr || C == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldc < N) return fail(FMM_ERR_INVALID_ARGUMENT, "ldc < N");
+  if (!aligned(P, 16)) return fail(FMM_ERR_MISALIGNED, "P must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (scheme) {
+    case FMM_SCHEME_RANK7: return launch_reconstruct<FMM_SCHEME_RANK7>(P, d, M, N, bias, C, ldc, s);
+    case FMM_SCHEME_RANK48: return launch_reconstruct<FMM_SCHEME_RANK48>(P, d, M, N, bias, C, ldc, s);
+    default: return launch_reconstruct<FMM_SCHEME_RANK49>(P, d, M, N, bias, C, ldc, s);
+  }
+}
+
+int fmm_linear(int scheme, const void* A, const void* W, const void* bias, void* C, int64_t M,
+               int64_t K, int64_t N, void* L, void* Rt, void* P, unsigned int flags,
+               fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, M, K, N, &d)) return rc;
+  if (A == nullptr || C == nullptr || L == nullptr || Rt == nullptr || P == nullptr)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  const bool prepacked = (flags & FMM_LINEAR_PREPACKED) != 0;
+  if (!prepacked && W == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null weight");
+  if (int rc = fmm_transform_a(scheme, A, M, K, K, L, stream)) return rc;
+  if (!prepacked) {
+    if (int rc = fmm_transform_w(scheme, W, N, K, K, Rt, stream)) return rc;
+  }
+  if (int rc = fmm_leaf_gemm(static_cast<int>(d.rank), L, Rt, d.bm, d.bn, d.bk, P, stream)) return rc;
+  return fmm_reconstruct(scheme, P, M, N, bias, C, N, stream);
+}
+
+int fmm_set_wait_timeout_ns(uint64_t timeout_ns) {
+  if (timeout_ns == 0) return fail(FMM_ERR_INVALID_ARGUMENT, "timeout must be positive");
+  g_timeout_ns = timeout_ns;
+  return FMM_OK;
+}
+
+int fmm_device_status(int device, uint32_t* status, uint32_t* site, int reset) {
+  if (status == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null status");
+  int previous = 0;
+  cudaError_t e = cudaGetDevice(&previous);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (device != previous && (e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  int rc = FMM_OK;
+  unsigned int value = 0, where = 0;
+  if ((e = cudaDeviceSynchronize()) != cudaSuccess) rc = cuda_fail(e, "cudaDeviceSynchronize");
+  if (rc == FMM_OK && (e = cudaMemcpyFromSymbol(&value, g_status, sizeof(value))) != cudaSuccess)
+    rc = cuda_fail(e, "read status");
+  if (rc == FMM_OK && (e = cudaMemcpyFromSymbol(&where, g_timeout_site, sizeof(where))) != cudaSuccess)
+    rc = cuda_fail(e, "read timeout site");
+  if (rc == FMM_OK && reset) {
+    const unsigned int zero = 0;
+    if ((e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero))) != cudaSuccess ||
+        (e = cudaMemcpyToSymbol(g_timeout_site, &zero, sizeof(zero))) != cudaSuccess)
+      rc = cuda_fail(e, "clear status");
+  }
+  if (device != previous) cudaSetDevice(previous);
+  *status = value;
+  if (site != nullptr) *site = where;
+  return rc;
+}
+
+int fmm_test_bounded_wait(uint64_t timeout_ns, fmm_stream_t stream) {
+  if (timeout_ns == 0 || timeout_ns > 10000000000ull)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "probe timeout must be in (0, 10 s]");
+  bounded_wait_probe_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(timeout_ns);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "bounded wait probe launch");
+  return FMM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,274 @@
+// Leaf products of the reduced-rank linear: R independent FP16 GEMMs
+//   P[r][m][n] = sum_k L[r][m][k] * Rt[r][n][k]
+// on the 5th-generation tensor cores (tcgen05) of sm_100a.
+//
+// Structure (one CTA per SM, persistent over the (r, tile_m, tile_n) grid):
+//   warp 0      TMA producer: 3-D tensor maps over the stacked planes, one
+//               128x64 L tile and one BNx64 Rt tile per stage (128-byte
+//               swizzle), STAGES-deep ring guarded by full/empty mbarriers.
+//   warp 1      MMA issuer (one elected thread): 4 x tcgen05.mma m128nBNk16
+//               per stage into an FP32 accumulator in tensor memory; two
+//               accumulators (2 x BN columns) so the epilogue of one tile
+//               overlaps the main loop of the next.  Also owns TMEM alloc.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, round to FP16,
+//               16-byte stores of P.
+// Out-of-range rows/columns/K are zero-filled by TMA, so ragged shapes need
+// no special casing in the main loop; the epilogue masks its stores.
+// Every wait is bounded (mbar_wait_bounded); on a timeout all roles unwind,
+// drain what they issued, and the CTA frees its tensor memory and returns.
+#pragma once
+
+#include "fmm_common.cuh"
+
+namespace fmm {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN, int STAGES>
+struct LeafGemmConfig {
+  static constexpr int kBN = BN;
+  static constexpr int kStages = STAGES;
+  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;  // 16 KiB
+  static constexpr uint32_t kBBytes = BN * kGemmBK * 2;       // 32 KiB at BN=256
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+  // tiles + 1 KiB slack for the 1024-byte alignment + barrier block
+  static constexpr size_t kSmemBytes = size_t(STAGES) * kStageBytes + 1024 + 256;
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+};
+
+struct LeafGemmParams {
+  int64_t bm, bn, bk;
+  int64_t ldp;
+  int32_t rank;
+  int32_t tiles_m, tiles_n;
+  int32_t group_m;
+  __half* P;
+  uint64_t timeout_ns;
+};
+
+// Tile t -> (r, tm, tn): batches in order, inside a batch groups of
+// `group_m` M-tiles sweep the N-tiles so concurrently running CTAs share L
+// rows and Rt columns in L2.
+__device__ __forceinline__ void leaf_tile_coords(const LeafGemmParams& p, int t, int& r, int& tm,
+                                                 int& tn) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  r = t / per_batch;
+  const int local = t - r * per_batch;
+  const int per_group = p.group_m * p.tiles_n;
+  const int group = local / per_group;
+  const int first_m = group * p.group_m;
+  const int group_rows = min(p.tiles_m - first_m, p.group_m);
+  const int in_group = local - group * per_group;
+  tm = first_m + in_group % group_rows;
+  tn = in_group / group_rows;
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    leaf_gemm_kernel(const __grid_constant__ CUtensorMap tmap_l,
+                     const __grid_constant__ CUtensorMap tmap_r, const LeafGemmParams p) {
+  constexpr int BN = Cfg::kBN;
+  constexpr int STAGES = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t a_base = base;
+  const uint32_t b_base = base + STAGES * Cfg::kABytes;
+  uint8_t* ctrl = smem + STAGES * Cfg::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ctrl);
+  const uint32_t full_bar = smem_u32(bars);                   // [STAGES]
+  const uint32_t empty_bar = smem_u32(bars + STAGES);         // [STAGES]
+  const uint32_t tfull_bar = smem_u32(bars + 2 * STAGES);     // [2]
+  const uint32_t tempty_bar = smem_u32(bars + 2 * STAGES + 2);  // [2]
+  const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar + 8 * s, 1);
+      mbar_init(empty_bar + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar + 8 * b, 1);
+      mbar_init(tempty_bar + 8 * b, 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmap_l);
+    prefetch_tmap(&tmap_r);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = p.rank * p.tiles_m * p.tiles_n;
+  const int k_blocks = static_cast<int>((p.bk + kGemmBK - 1) / kGemmBK);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int r, tm, tn;
+        leaf_tile_coords(p, t, r, tm, tn);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait_bounded(empty_bar + 8 * stage, phase ^ 1u, abort, p.timeout_ns, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar + 8 * stage, Cfg::kStageBytes);
+          tma_load_3d(a_base + stage * Cfg::kABytes, &tmap_l, full_bar + 8 * stage,
+                      kb * kGemmBK, tm * kGemmBM, r);
+          tma_load_3d(b_base + stage * Cfg::kBBytes, &tmap_r, full_bar + 8 * stage,
+                      kb * kGemmBK, tn * BN, r);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // drain: the last min(STAGES, issued) loads may still be landing
+        int s = stage;
+        uint32_t ph = phase;
+        for (int n = 0; n < STAGES && n < issued; ++n) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1u;
+          }
+          volatile int no_abort = 0;
+          mbar_wait_bounded(full_bar + 8 * s, ph, &no_abort, p.timeout_ns, 5);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait_bounded(tempty_bar + 8 * acc, acc_phase ^ 1u, abort, p.timeout_ns, 2)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait_bounded(full_bar + 8 * stage, phase, abort, p.timeout_ns, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = a_base + stage * Cfg::kABytes;
+          const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            const uint64_t a_desc = smem_desc_k_sw128(a_addr + kk * 32);
+            const uint64_t b_desc = smem_desc_k_sw128(b_addr + kk * 32);
+            tc_mma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          tc_commit(empty_bar + 8 * stage);  // frees the stage once read
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(tfull_bar + 8 * acc);  // accumulator ready for the epilogue
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        // drain our own tensor-core work before the CTA frees TMEM
+        tc_commit(drain_bar);
+        volatile int no_abort = 0;
+        mbar_wait_bounded(drain_bar, 0, &no_abort, p.timeout_ns, 6);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      int r, tm, tn;
+      leaf_tile_coords(p, t, r, tm, tn);
+      int ready = 0;
+      if (lane == 0)
+        ready = mbar_wait_bounded(tfull_bar + 8 * acc, acc_phase, abort, p.timeout_ns, 4) ? 1 : 0;
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * kGemmBM + row_in_tile;
+      __half* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
+      const uint32_t t_addr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tc_ld_32x32b_x32(t_addr + c, v);
+        tc_wait_ld();
+        const int64_t col = static_cast<int64_t>(tn) * BN + c;
+        if (row < p.bm) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int64_t c8 = col + q * 8;
+            if (c8 + 8 <= p.ldp) {
+              uint4 pk;
+              __half2* h = reinterpret_cast<__half2*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                h[e] = __floats2half2_rn(__uint_as_float(v[q * 8 + 2 * e]),
+                                         __uint_as_float(v[q * 8 + 2 * e + 1]));
+              *reinterpret_cast<uint4*>(prow + c8) = pk;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar + 8 * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace fmm

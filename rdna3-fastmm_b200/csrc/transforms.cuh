@@ -1,0 +1,209 @@
+// Block transforms (HBM-bound streaming kernels) for the reduced-rank linear.
+//
+// The scheme-specific arithmetic comes from generated/fmm_schemes.cuh; this
+// file supplies the vector type it runs on, the block addressing with zero
+// padding, and the stores.  Every kernel reads each source element once and
+// writes each destination element once, with 8- or 16-byte vector accesses on
+// the aligned fast path.
+#pragma once
+
+#include "fmm_common.cuh"
+
+namespace fmm {
+
+template <int N>
+struct VecF {
+  float v[N];
+};
+
+// One FP32 rounding per certificate operation; the _rn intrinsics keep the
+// compiler from contracting or reassociating anything.
+template <int N>
+__device__ __forceinline__ VecF<N> vadd(const VecF<N>& a, const VecF<N>& b) {
+  VecF<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = __fadd_rn(a.v[i], b.v[i]);
+  return r;
+}
+template <int N>
+__device__ __forceinline__ VecF<N> vsub(const VecF<N>& a, const VecF<N>& b) {
+  VecF<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = __fsub_rn(a.v[i], b.v[i]);
+  return r;
+}
+// Unary minus as 0 - x: a zero operand yields +0, matching the reference's
+// Triton kernels (they lower `-x` to a subtraction from zero).
+template <int N>
+__device__ __forceinline__ VecF<N> vneg(const VecF<N>& a) {
+  VecF<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = __fsub_rn(0.0f, a.v[i]);
+  return r;
+}
+// Scaling by a power of two (or a small dyadic): exact, so x/2 == x*0.5.
+template <int N>
+__device__ __forceinline__ VecF<N> vscale(const VecF<N>& a, float c) {
+  VecF<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = __fmul_rn(a.v[i], c);
+  return r;
+}
+
+template <int N>
+struct VecIO;
+
+template <>
+struct VecIO<4> {
+  using BF = uint2;   // 4 x bf16
+  using H = uint2;    // 4 x fp16
+};
+template <>
+struct VecIO<8> {
+  using BF = uint4;
+  using H = uint4;
+};
+
+template <int N>
+__device__ __forceinline__ VecF<N> load_bf16_vec(const __nv_bfloat16* p) {
+  typename VecIO<N>::BF raw = __ldg(reinterpret_cast<const typename VecIO<N>::BF*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  VecF<N> r;
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    r.v[2 * i] = f.x;
+    r.v[2 * i + 1] = f.y;
+  }
+  return r;
+}
+
+template <int N>
+__device__ __forceinline__ VecF<N> load_half_vec(const __half* p) {
+  typename VecIO<N>::H raw = *reinterpret_cast<const typename VecIO<N>::H*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+  VecF<N> r;
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    float2 f = __half22float2(h[i]);
+    r.v[2 * i] = f.x;
+    r.v[2 * i + 1] = f.y;
+  }
+  return r;
+}
+
+template <int N>
+__device__ __forceinline__ void store_half_vec(__half* p, const VecF<N>& x) {
+  typename VecIO<N>::H raw;
+  __half2* h = reinterpret_cast<__half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) h[i] = __floats2half2_rn(x.v[2 * i], x.v[2 * i + 1]);
+  *reinterpret_cast<typename VecIO<N>::H*>(p) = raw;
+}
+
+template <int N>
+__device__ __forceinline__ void store_bf16_vec(__nv_bfloat16* p, const VecF<N>& x) {
+  typename VecIO<N>::BF raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) h[i] = __floats2bfloat162_rn(x.v[2 * i], x.v[2 * i + 1]);
+  *reinterpret_cast<typename VecIO<N>::BF*>(p) = raw;
+}
+
+// ---------------------------------------------------------------------------
+// Input-side transform: src [rows, cols] BF16 (leading dim ld) is cut into
+// S x S zero-padded blocks of [brows, bcols]; Prog combines them into
+// Prog::kOutputs FP16 planes dst[o][brows][ldd].
+//
+// kWeight = false: activation side, input q is block (q / S, q % S) of A.
+// kWeight = true : weight side; the program's input q is block (q / S, q % S)
+//                  of B = weight^T, which is block (q % S, q / S) of weight,
+//                  and rows/cols here are weight's (N, K).  The planes come out
+//                  as Rt[r][n][k], the K-major transpose of the reference's
+//                  Rw[r][k][n], without any transposition in memory.
+//
+// Thread mapping: one thread per VEC consecutive plane columns of one plane
+// row; consecutive threads take consecutive vectors, so every block load and
+// plane store of a warp is one contiguous span.  Columns in [bcols, ldd) are
+// padding and are written as zeros.
+template <class Prog, int S, int VEC, bool kWeight>
+__global__ void __launch_bounds__(256) block_transform_kernel(
+    const __nv_bfloat16* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
+    __half* __restrict__ dst, int64_t brows, int64_t bcols, int64_t ldd, int vector_loads) {
+  const int64_t plane = brows * ldd;
+  const uint32_t vecs_per_row = static_cast<uint32_t>(ldd / VEC);
+  const uint32_t total = static_cast<uint32_t>(brows) * vecs_per_row;
+  for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += gridDim.x * blockDim.x) {
+    const uint32_t i = idx / vecs_per_row;
+    const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
+    auto in = [&](int q) -> VecF<VEC> {
+      const int br = kWeight ? (q % S) : (q / S);
+      const int bc = kWeight ? (q / S) : (q % S);
+      const int64_t r = br * brows + i;
+      const int64_t c0 = bc * bcols + j;
+      VecF<VEC> x;
+      if (vector_loads && r < rows && j + VEC <= bcols && c0 + VEC <= cols) {
+        x = load_bf16_vec<VEC>(src + r * ld + c0);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const bool ok = r < rows && j + e < bcols && c0 + e < cols;
+          x.v[e] = ok ? __bfloat162float(src[r * ld + c0 + e]) : 0.0f;
+        }
+      }
+      return x;
+    };
+    auto out = [&](int o, const VecF<VEC>& x) {
+      store_half_vec<VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
+    };
+    Prog::template run<VecF<VEC>>(in, out);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Output side (unfused reconstruct): P[r][bm][ldp] FP16 -> C[M,N] BF16.
+// Output o is C block (o / S, o % S); bias[bc*bn + c] is added after the whole
+// recombination, then rounded to nearest even BF16.
+template <class Prog, int S, int VEC>
+__global__ void __launch_bounds__(256) reconstruct_kernel(
+    const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
+    const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ C, int64_t M, int64_t N,
+    int64_t ldc, int vector_stores) {
+  const int64_t plane = bm * ldp;
+  const uint32_t vecs_per_row = static_cast<uint32_t>((bn + VEC - 1) / VEC);
+  const uint32_t total = static_cast<uint32_t>(bm) * vecs_per_row;
+  for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += gridDim.x * blockDim.x) {
+    const uint32_t i = idx / vecs_per_row;
+    const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
+    auto in = [&](int r) -> VecF<VEC> {
+      return load_half_vec<VEC>(P + r * plane + static_cast<int64_t>(i) * ldp + j);
+    };
+    auto out = [&](int o, const VecF<VEC>& x) {
+      const int br = o / S, bc = o % S;
+      const int64_t row = br * bm + i;
+      if (row >= M) return;
+      const int64_t c0 = bc * bn + j;
+      VecF<VEC> y = x;
+      if (bias != nullptr) {
+        VecF<VEC> b;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          b.v[e] = (j + e < bn && c0 + e < N) ? __bfloat162float(bias[c0 + e]) : 0.0f;
+        y = vadd(x, b);
+      }
+      __nv_bfloat16* dst = C + row * ldc + c0;
+      if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
+        store_bf16_vec<VEC>(dst, y);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (j + e < bn && c0 + e < N) dst[e] = __float2bfloat16_rn(y.v[e]);
+      }
+    };
+    Prog::template run<VecF<VEC>>(in, out);
+  }
+}
+
+}  // namespace fmm

@@ -1,0 +1,162 @@
+"""ctypes binding of ``libfmm_sm100.so`` (declared in ``include/fmm_sm100.h``).
+
+The library is built in-tree (``rdna3-fastmm_b200/build.py``) into
+``rdna3_fastmm/_lib``.  There is no fallback: when the library is missing, or
+a call fails, the error is raised to the caller.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from functools import lru_cache
+from pathlib import Path
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "_lib" / "libfmm_sm100.so"
+
+FMM_OK = 0
+FMM_ERR_INVALID_ARGUMENT = 1
+FMM_ERR_MISALIGNED = 2
+FMM_ERR_UNSUPPORTED = 3
+FMM_ERR_CUDA = 4
+FMM_ERR_DEVICE_TIMEOUT = 5
+FMM_ERR_TOO_LARGE = 6
+FMM_STATUS_TIMEOUT = 1
+FMM_LINEAR_PREPACKED = 1
+
+SCHEME_IDS = {"rank7": 7, "rank48": 48, "rank49": 49}
+
+
+class NativeLibraryError(RuntimeError):
+    """The sm_100a library is missing, not loadable, or a call failed."""
+
+
+class FmmDims(ctypes.Structure):
+    _fields_ = [
+        ("scheme_size", ctypes.c_int64),
+        ("rank", ctypes.c_int64),
+        ("bm", ctypes.c_int64),
+        ("bk", ctypes.c_int64),
+        ("bn", ctypes.c_int64),
+        ("ldk", ctypes.c_int64),
+        ("ldp", ctypes.c_int64),
+        ("left_elements", ctypes.c_int64),
+        ("right_elements", ctypes.c_int64),
+        ("product_elements", ctypes.c_int64),
+    ]
+
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_SIGNATURES = {
+    "fmm_version": ([], ctypes.c_int),
+    "fmm_last_error_string": ([], ctypes.c_char_p),
+    "fmm_plan_dims": ([ctypes.c_int, _I64, _I64, _I64, ctypes.POINTER(FmmDims)], ctypes.c_int),
+    "fmm_transform_a": ([ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_transform_w": ([ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_leaf_gemm": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_reconstruct": ([ctypes.c_int, _P, _I64, _I64, _P, _P, _I64, _P], ctypes.c_int),
+    "fmm_linear": (
+        [ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, ctypes.c_uint, _P],
+        ctypes.c_int,
+    ),
+    "fmm_set_wait_timeout_ns": ([ctypes.c_uint64], ctypes.c_int),
+    "fmm_device_status": (
+        [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32), ctypes.c_int],
+        ctypes.c_int,
+    ),
+    "fmm_test_bounded_wait": ([ctypes.c_uint64, _P], ctypes.c_int),
+}
+
+
+@lru_cache(maxsize=None)
+def library() -> ctypes.CDLL:
+    if not LIBRARY_PATH.exists():
+        raise NativeLibraryError(
+            f"{LIBRARY_PATH} is missing; build it with `python rdna3-fastmm_b200/build.py`"
+        )
+    try:
+        lib = ctypes.CDLL(str(LIBRARY_PATH))
+    except OSError as error:
+        raise NativeLibraryError(f"cannot load {LIBRARY_PATH}: {error}") from error
+    for name, (args, result) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = result
+    return lib
+
+
+def last_error() -> str:
+    raw = library().fmm_last_error_string()
+    return raw.decode() if raw else ""
+
+
+def check(code: int, what: str) -> None:
+    if code == FMM_OK:
+        return
+    message = f"{what}: {last_error()} (libfmm_sm100 error {code})"
+    if code in (FMM_ERR_INVALID_ARGUMENT, FMM_ERR_MISALIGNED, FMM_ERR_UNSUPPORTED, FMM_ERR_TOO_LARGE):
+        raise ValueError(message)
+    raise NativeLibraryError(message)
+
+
+def plan_dims(scheme: str, rows: int, inner: int, columns: int) -> FmmDims:
+    dims = FmmDims()
+    check(library().fmm_plan_dims(SCHEME_IDS[scheme], rows, inner, columns, ctypes.byref(dims)),
+          "fmm_plan_dims")
+    return dims
+
+
+def _ptr(tensor) -> int | None:
+    return None if tensor is None else tensor.data_ptr()
+
+
+def _stream(device) -> int:
+    import torch
+
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def transform_a(scheme: str, A, L) -> None:
+    M, K = A.shape
+    check(library().fmm_transform_a(SCHEME_IDS[scheme], _ptr(A), M, K, A.stride(0), _ptr(L),
+                                    _stream(A.device)), "fmm_transform_a")
+
+
+def transform_w(scheme: str, W, Rt) -> None:
+    N, K = W.shape
+    check(library().fmm_transform_w(SCHEME_IDS[scheme], _ptr(W), N, K, W.stride(0), _ptr(Rt),
+                                    _stream(W.device)), "fmm_transform_w")
+
+
+def leaf_gemm(rank: int, L, Rt, bm: int, bn: int, bk: int, P) -> None:
+    check(library().fmm_leaf_gemm(rank, _ptr(L), _ptr(Rt), bm, bn, bk, _ptr(P), _stream(L.device)),
+          "fmm_leaf_gemm")
+
+
+def reconstruct(scheme: str, P, M: int, N: int, bias, C) -> None:
+    check(library().fmm_reconstruct(SCHEME_IDS[scheme], _ptr(P), M, N, _ptr(bias), _ptr(C),
+                                    C.stride(0), _stream(P.device)), "fmm_reconstruct")
+
+
+def linear(scheme: str, A, W, bias, C, L, Rt, P, prepacked: bool) -> None:
+    M, K = A.shape
+    N = C.shape[1]
+    flags = FMM_LINEAR_PREPACKED if prepacked else 0
+    check(library().fmm_linear(SCHEME_IDS[scheme], _ptr(A), _ptr(W), _ptr(bias), _ptr(C), M, K, N,
+                               _ptr(L), _ptr(Rt), _ptr(P), flags, _stream(A.device)), "fmm_linear")
+
+
+def set_wait_timeout_ns(timeout_ns: int) -> None:
+    check(library().fmm_set_wait_timeout_ns(timeout_ns), "fmm_set_wait_timeout_ns")
+
+
+def device_status(device_index: int, reset: bool = False) -> tuple[int, int]:
+    status = ctypes.c_uint32(0)
+    site = ctypes.c_uint32(0)
+    check(library().fmm_device_status(device_index, ctypes.byref(status), ctypes.byref(site),
+                                      int(reset)), "fmm_device_status")
+    return status.value, site.value
+
+
+def test_bounded_wait(timeout_ns: int, device) -> None:
+    check(library().fmm_test_bounded_wait(timeout_ns, _stream(device)), "fmm_test_bounded_wait")
