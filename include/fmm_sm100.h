@@ -112,6 +112,27 @@ int fmm_linear(int scheme, const void* A, const void* W, const void* bias, void*
                int64_t K, int64_t N, void* L, void* Rt, void* P, unsigned int flags,
                fmm_stream_t stream);
 
+/* Size of the fixed scratch array behind fmm_linear_noalloc (32 MiB). */
+#define FMM_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* fmm_linear without caller planes and without any allocation: for callers
+ * that are handed device buffers for A, weight, bias and C but cannot
+ * allocate device memory themselves -- a plugin whose host application owns
+ * and budgets all device memory, or a loop that must never call cudaMalloc
+ * because cudaMalloc can synchronise the device.  The L, Rt and P planes live
+ * in one fixed FMM_NOALLOC_SCRATCH_BYTES array inside this library, which
+ * every GPU that loads the library keeps until the process exits; shapes
+ * whose planes do not fit (see fmm_plan_dims) return FMM_ERR_TOO_LARGE.
+ * The first call on a device looks up that array's device address (with the
+ * device current); make that first call before any stream capture.  All
+ * calls on a device share the one array, so calls that overlap on the GPU
+ * (on different streams, or from different threads) race; serialise them.
+ * Nothing in the array has to start at zero: each call writes every plane
+ * element it later reads.  No counterpart in the reference (its Python plans
+ * always allocate through PyTorch). */
+int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bias, void* C,
+                       int64_t M, int64_t K, int64_t N, fmm_stream_t stream);
+
 /* Upper bound, in nanoseconds, of every device-side wait (default 2 s).  A
  * wait that runs out records FMM_STATUS_TIMEOUT and unwinds the kernel.  No
  * counterpart in the reference (it has no device-side waits). */

@@ -17,6 +17,11 @@
 #include "generated/fmm_schemes.cuh"
 #include "leaf_gemm.cuh"
 
+// Scratch of fmm_linear_noalloc: the L, Rt and P planes of one call live in
+// this array instead of caller-provided buffers.  It is part of the module, so
+// every GPU that loads this library holds it until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[FMM_NOALLOC_SCRATCH_BYTES];
+
 namespace fmm {
 
 namespace {
@@ -74,6 +79,7 @@ int dims_for(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* d) {
 struct DeviceInfo {
   int sm_count = 0;
   bool gemm_configured = false;
+  void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch
 };
 
 constexpr int kMaxDevices = 64;
@@ -254,6 +260,23 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   return FMM_OK;
 }
 
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  DeviceInfo* info = nullptr;
+  if (int rc = device_info(&info)) return rc;
+  std::lock_guard<std::mutex> lock(g_device_mutex);
+  if (info->noalloc_scratch == nullptr) {
+    void* address = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&address, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    info->noalloc_scratch = address;
+  }
+  *out = info->noalloc_scratch;
+  return FMM_OK;
+}
+
 __global__ void bounded_wait_probe_kernel(uint64_t timeout_ns) {
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
@@ -359,6 +382,31 @@ int fmm_linear(int scheme, const void* A, const void* W, const void* bias, void*
   }
   if (int rc = fmm_leaf_gemm(static_cast<int>(d.rank), L, Rt, d.bm, d.bn, d.bk, P, stream)) return rc;
   return fmm_reconstruct(scheme, P, M, N, bias, C, N, stream);
+}
+
+int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bias, void* C,
+                       int64_t M, int64_t K, int64_t N, fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, M, K, N, &d)) return rc;
+  if (A == nullptr || W == nullptr || C == nullptr)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  const int64_t left = round_up(d.left_elements * 2, 256);
+  const int64_t right = round_up(d.right_elements * 2, 256);
+  const int64_t products = round_up(d.product_elements * 2, 256);
+  const int64_t needed = left + right + products;
+  if (needed > static_cast<int64_t>(FMM_NOALLOC_SCRATCH_BYTES))
+    return fail(FMM_ERR_TOO_LARGE,
+                "fmm_linear_noalloc: this shape needs " + std::to_string(needed) +
+                    " bytes of scratch, more than its fixed " +
+                    std::to_string(static_cast<long long>(FMM_NOALLOC_SCRATCH_BYTES)) +
+                    "; use fmm_linear with caller-provided planes");
+  void* base = nullptr;
+  if (int rc = noalloc_scratch(&base)) return rc;
+  unsigned char* bytes = static_cast<unsigned char*>(base);
+  // Every plane element the GEMM and the reconstruct read is written earlier
+  // in the same call (pitch padding included), so nothing is cleared first.
+  return fmm_linear(scheme, A, W, bias, C, M, K, N, bytes, bytes + left, bytes + left + right, 0u,
+                    stream);
 }
 
 int fmm_set_wait_timeout_ns(uint64_t timeout_ns) {

@@ -59,6 +59,7 @@ _SIGNATURES = {
         [ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, ctypes.c_uint, _P],
         ctypes.c_int,
     ),
+    "fmm_linear_noalloc": ([ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P], ctypes.c_int),
     "fmm_set_wait_timeout_ns": ([ctypes.c_uint64], ctypes.c_int),
     "fmm_device_status": (
         [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32), ctypes.c_int],
@@ -144,6 +145,14 @@ def linear(scheme: str, A, W, bias, C, L, Rt, P, prepacked: bool) -> None:
     flags = FMM_LINEAR_PREPACKED if prepacked else 0
     check(library().fmm_linear(SCHEME_IDS[scheme], _ptr(A), _ptr(W), _ptr(bias), _ptr(C), M, K, N,
                                _ptr(L), _ptr(Rt), _ptr(P), flags, _stream(A.device)), "fmm_linear")
+
+
+def linear_noalloc(scheme: str, A, W, bias, C) -> int:
+    """Raw return code of fmm_linear_noalloc (callers decide how to react)."""
+    M, K = A.shape
+    N = C.shape[1]
+    return library().fmm_linear_noalloc(SCHEME_IDS[scheme], _ptr(A), _ptr(W), _ptr(bias), _ptr(C),
+                                        M, K, N, _stream(A.device))
 
 
 def set_wait_timeout_ns(timeout_ns: int) -> None:
