@@ -186,18 +186,35 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     from rdna3_fastmm.runtime import Rank7Plan, Rank48Plan, Rank49Plan
 
     plans = {"rank7": Rank7Plan, "rank48": Rank48Plan, "rank49": Rank49Plan}
-    scheme, M, K, N, with_bias, prepacked, description = WORKLOADS[args.workload]
+    scheme, M_total, K, N, with_bias, prepacked, description = WORKLOADS[args.workload]
     if args.rows:
-        M = args.rows
-        description += f" (rows overridden to {M})"
+        M_total = args.rows
+        description += f" (rows overridden to {M_total})"
+    shard = args.shard and world > 1
+    if shard:
+        from rdna3_fastmm.distributed import shard_rows
+
+        row_start, M = shard_rows(M_total, world)[rank]
+        padded = -(-M_total // world)
+        description += f"; rows sharded over {world} GPUs, output all-gathered (NCCL)"
+    else:
+        M = M_total
     plan = plans[scheme](M, K, N, device, dtype=torch.bfloat16, compute_dtype=torch.float16)
+    # every rank draws its own rows (seeded by rank), the weight is replicated
     A_h, W_h, b_h = make_linear_inputs(M, K, N, seed=0, bias=with_bias)
+    if shard and rank:
+        A_h = make_linear_inputs(M, K, 1, seed=100 + rank)[0]
     A, W = A_h.to(device), W_h.to(device)
     bias = b_h.to(device) if b_h is not None else None
     ws = plan.allocate_workspace(0.9, prepacked_right=prepacked)
     packed = plan.pack_weight(W, 0.9) if prepacked else None
     right = packed.transformed if prepacked else ws.right_transformed
-    out = torch.empty((M, N), device=device, dtype=torch.bfloat16)
+    if shard:
+        gathered = torch.empty((world * padded, N), device=device, dtype=torch.bfloat16)
+        slot = gathered[rank * padded:(rank + 1) * padded]
+        out = slot[:M]
+    else:
+        out = torch.empty((M, N), device=device, dtype=torch.bfloat16)
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
     s = plan.shape
     stream = torch.cuda.current_stream(device)
@@ -214,6 +231,9 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         ev[3].record(stream)
         _native.reconstruct(scheme, ws.products, M, N, bias, out)
         ev[4].record(stream)
+        if shard:
+            dist.all_gather_into_tensor(gathered, slot)
+        ev[5].record(stream)
 
     def barrier():
         if world > 1:
@@ -221,9 +241,9 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
 
     for _ in range(args.warmup):
         flush.zero_()
-        step([torch.cuda.Event(enable_timing=True) for _ in range(5)])
+        step([torch.cuda.Event(enable_timing=True) for _ in range(6)])
     torch.cuda.synchronize(device)
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize(device)
     with ClockSampler(device.index) as clocks:
@@ -232,14 +252,15 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
             step(ev)
         torch.cuda.synchronize(device)
         barrier()
-    stages = {"transform_a": [], "transform_w": [], "leaf_gemm": [], "reconstruct": []}
+    stages = {"transform_a": [], "transform_w": [], "leaf_gemm": [], "reconstruct": [], "all_gather": []}
     totals = []
     for ev in events:
         stages["transform_a"].append(ev[0].elapsed_time(ev[1]))
         stages["transform_w"].append(ev[1].elapsed_time(ev[2]))
         stages["leaf_gemm"].append(ev[2].elapsed_time(ev[3]))
         stages["reconstruct"].append(ev[3].elapsed_time(ev[4]))
-        totals.append(ev[0].elapsed_time(ev[4]))
+        stages["all_gather"].append(ev[4].elapsed_time(ev[5]))
+        totals.append(ev[0].elapsed_time(ev[5]))
     total_ms = sum(totals)
     status, _ = _native.device_status(device.index)
     if status:
@@ -282,13 +303,21 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     A_d, W_d = torch.empty_like(A), torch.empty_like(W)
     b_d = torch.empty_like(bias) if bias is not None else None
 
+    if shard:
+        from rdna3_fastmm.distributed import RowShardedLinear
+
+        layer = RowShardedLinear(plans[scheme], M_total, W, bias=bias, max_free_memory_fraction=0.9)
+        C_pin = torch.empty((world * padded, N), dtype=torch.bfloat16).pin_memory()
+
     def e2e_step():
         A_d.copy_(A_pin, non_blocking=True)
         if not prepacked:
             W_d.copy_(W_pin, non_blocking=True)
         if b_d is not None:
             b_d.copy_(b_pin, non_blocking=True)
-        if prepacked:
+        if shard:
+            res = layer(A_d, out=gathered)
+        elif prepacked:
             res = plan.run_linear_packed(A_d, packed, ws, b_d, out)
         else:
             res = plan.run_linear(A_d, W_d, ws, b_d, out)
@@ -308,7 +337,7 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     h2d = A_h.numel() * 2 + (0 if prepacked else W_h.numel() * 2) + (N * 2 if b_h is not None else 0)
-    d2h = M * N * 2
+    d2h = C_pin.numel() * 2
 
     local = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
@@ -317,7 +346,8 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     if rank != 0:
         return None
 
-    flops = 2.0 * M * N * K
+    flops = 2.0 * M * N * K  # this rank's share
+    job_flops = 2.0 * M_total * N * K if shard else world * flops
     ms_per_step = total_ms / args.steps
     pk, pk_kind = peaks()
     leaf_flops = 2.0 * plan.rank * s.block_rows * s.block_inner * s.block_columns
@@ -344,24 +374,30 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
                       "frac": round(achieved / peak, 3), "flops": leaf_flops},
         "reconstruct": hbm(r_bytes, statistics.mean(stages["reconstruct"])),
     }
+    if shard:
+        gather_ms = statistics.mean(stages["all_gather"])
+        moved = (world - 1) * padded * N * 2  # bytes each rank receives
+        kernels["all_gather"] = {"ms": round(gather_ms, 4), "bytes_received": moved,
+                                 "gbs": round(moved / (gather_ms * 1e-3) / 1e9, 1) if gather_ms > 0 else None}
     traffic = profile_traffic(args.workload)
     line = {
         "metric": "effective TFLOP/s (2MNK/t) per B200 and at 8 GPUs; speedup vs cuBLAS BF16",
-        "value": round(world * flops / (ms_per_step * 1e-3) / 1e12, 2),
+        "value": round(job_flops / (ms_per_step * 1e-3) / 1e12, 2),
         "unit": "TFLOP/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if shard else "weak",
         "vs_baseline": None,
         "dtype": "bf16 in/out, fp16 leaves, fp32 accumulate",
         "data": "synthetic (seeded A~N(0,1), W~N(0,0.02) BF16)",
         "config": {"workload": f"{args.workload}: {description}", "scheme": scheme,
                    "M": M, "K": K, "N": N, "bias": with_bias, "prepacked": prepacked,
                    "l2": "flushed (256 MiB write) before every step",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+                   "parallelism": (f"rows sharded x{world} + NCCL all-gather" if shard else
+                                   f"replicas x{world}" if world > 1 else "single GPU")},
         "roofline": {"bound": "tensor", "kernel": "leaf_gemm", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 3),
                      "peak_source": f"{pk_kind} bf16_tflops_sustained (dense FP16 == BF16 rate)",
@@ -372,9 +408,10 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
                         "speedup": round(cublas_ms / ms_per_step, 3)},
         "accuracy": {"rel_l2_vs_fp64": rel, "native_bf16_rel_l2": native_rel,
                      "ratio": rel / native_rel if native_rel else None, "sampled_rows": int(rows.numel())},
-        "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+        "e2e": {"value": round(job_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": f"{type(plan).__name__}.run_linear{'_packed' if prepacked else ''}"},
+                "api": ("RowShardedLinear (gather)" if shard else
+                f"{type(plan).__name__}.run_linear{'_packed' if prepacked else ''}")},
         "clocks": clocks.summary(),
         "gpu_launches": args.steps * (3 if prepacked else 4),
     }
@@ -391,6 +428,8 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--rows", type=int, default=0,
                         help="override M (smaller cases for profiler captures)")
+    parser.add_argument("--shard", action="store_true",
+                        help="split M over the ranks and all-gather C (strong scaling)")
     parser.add_argument("--profile", action="store_true",
                         help="timed steps only: no cuBLAS, e2e, parity or CPU legs")
     args = parser.parse_args()

@@ -1,0 +1,86 @@
+"""Host logic of the row-sharded linear on 2 CPU ranks (gloo): sharding
+arithmetic, in-place all-gather assembly, and a failed rank turning into an
+error on its peer instead of a hang.  The B200 plan is replaced by
+``F.linear`` on the CPU (the product is never exercised here)."""
+
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from rdna3_fastmm.distributed import RowShardedLinear, shard_rows
+
+
+def test_shard_rows_even_and_uneven():
+    assert shard_rows(8192, 4) == [(0, 2048), (2048, 2048), (4096, 2048), (6144, 2048)]
+    assert shard_rows(10, 4) == [(0, 3), (3, 3), (6, 2), (8, 2)]
+    assert sum(c for _, c in shard_rows(65537, 8)) == 65537
+    with pytest.raises(ValueError):
+        shard_rows(0, 2)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, rows, mode, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    try:
+        g = torch.Generator().manual_seed(0)
+        A = torch.randn((rows, 16), generator=g).to(torch.bfloat16)
+        W = torch.randn((24, 16), generator=g).to(torch.bfloat16)
+
+        def local(x, out):
+            out.copy_(torch.nn.functional.linear(x, W))
+
+        layer = RowShardedLinear(None, rows, W, local_linear=local)
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("rank 1 leaves before the collective")
+        try:
+            full = layer(layer.local_rows(A))
+            mine = layer(layer.local_rows(A), gather=False)
+            expected = torch.nn.functional.linear(A, W)
+            results[rank] = bool(torch.equal(full, expected)) and bool(
+                torch.equal(mine, expected[layer.shard.start:layer.shard.start + layer.shard.count]))
+        except RuntimeError as error:  # the peer is gone: the collective errors out
+            results[rank] = f"error: {type(error).__name__}"
+    except RuntimeError:
+        results[rank] = "left"
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run(world, rows, mode):
+    ctx = mp.get_context("spawn")
+    results = ctx.Manager().dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, rows, mode, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert not p.is_alive(), "a rank hung"
+    return dict(results)
+
+
+@pytest.mark.parametrize("rows", [64, 37])
+def test_two_rank_gather_matches_full_linear(rows):
+    results = _run(2, rows, "ok")
+    assert results == {0: True, 1: True}
+
+
+def test_failed_rank_becomes_an_error_not_a_hang():
+    results = _run(2, 64, "fail")
+    assert results[1] == "left"
+    assert str(results[0]).startswith("error")
