@@ -8,6 +8,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -79,6 +80,9 @@ int dims_for(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* d) {
 struct DeviceInfo {
   int sm_count = 0;
   bool gemm_configured = false;
+  bool pair256_configured = false;
+  bool pair128_configured = false;
+  bool pair192_configured = false;
   void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch
 };
 
@@ -109,6 +113,9 @@ int device_info(DeviceInfo** out) {
 }
 
 // ------------------------------------------------------------------ dispatch
+// Launch shapes were swept on B200 with random data (threads per block,
+// minimum resident blocks, grid cap in blocks per SM); with every input
+// preloaded these reach 91-98 % of the measured copy bandwidth.
 template <int SCHEME>
 struct SchemeTraits;
 template <>
@@ -118,6 +125,8 @@ struct SchemeTraits<FMM_SCHEME_RANK7> {
   using Output = gen::Rank7Output;
   static constexpr int S = 2;
   static constexpr int VEC = 8;
+  static constexpr int kInThreads = 256, kInBlocks = 1, kInGrid = 64;
+  static constexpr int kOutVec = 8, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 64;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK48> {
@@ -126,6 +135,8 @@ struct SchemeTraits<FMM_SCHEME_RANK48> {
   using Output = gen::Rank48Output;
   static constexpr int S = 4;
   static constexpr int VEC = 4;
+  static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
+  static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 16;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK49> {
@@ -134,11 +145,13 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
   using Output = gen::Rank49Output;
   static constexpr int S = 4;
   static constexpr int VEC = 4;
+  static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
+  static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 16;
 };
 
-int streaming_grid(const DeviceInfo* info, int64_t work_items) {
-  const int64_t blocks = ceil_div(work_items, 256);
-  const int64_t cap = int64_t(info->sm_count) * 16;
+int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int blocks_per_sm) {
+  const int64_t blocks = ceil_div(work_items, threads);
+  const int64_t cap = int64_t(info->sm_count) * blocks_per_sm;
   return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 
@@ -151,8 +164,8 @@ int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t 
   const bool vec = (bcols % T::VEC == 0) && (ld % T::VEC == 0) && aligned(src, 2 * T::VEC);
   const int64_t items = brows * (ldd / T::VEC);
   using Prog = typename std::conditional<kWeight, typename T::Right, typename T::Left>::type;
-  block_transform_kernel<Prog, T::S, T::VEC, kWeight>
-      <<<streaming_grid(info, items), 256, 0, stream>>>(
+  block_transform_kernel<Prog, T::S, T::VEC, kWeight, T::kInThreads, T::kInBlocks>
+      <<<streaming_grid(info, items, T::kInThreads, T::kInGrid), T::kInThreads, 0, stream>>>(
           static_cast<const __nv_bfloat16*>(src), rows, cols, ld, static_cast<__half*>(dst), brows,
           bcols, ldd, vec ? 1 : 0);
   cudaError_t e = cudaGetLastError();
@@ -164,12 +177,13 @@ template <int SCHEME>
 int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                        void* C, int64_t ldc, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
+  constexpr int V = T::kOutVec;
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
-  const bool vec = (d.bn % T::VEC == 0) && (ldc % T::VEC == 0) && aligned(C, 2 * T::VEC);
-  const int64_t items = d.bm * ceil_div(d.bn, T::VEC);
-  reconstruct_kernel<typename T::Output, T::S, T::VEC>
-      <<<streaming_grid(info, items), 256, 0, stream>>>(
+  const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
+  const int64_t items = d.bm * ceil_div(d.bn, V);
+  reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks>
+      <<<streaming_grid(info, items, T::kOutThreads, T::kOutGrid), T::kOutThreads, 0, stream>>>(
           static_cast<const __half*>(P), d.bm, d.bn, d.ldp,
           static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(C), M, N, ldc,
           vec ? 1 : 0);
@@ -217,6 +231,89 @@ int plane_map(CUtensorMap* map, const void* base, int64_t k, int64_t rows, int64
 }
 
 using GemmCfg = LeafGemmConfig<256, 4>;
+using PairCfg256 = LeafGemmPairConfig<256, 6>;
+using PairCfg192 = LeafGemmPairConfig<192, 7>;
+using PairCfg128 = LeafGemmPairConfig<128, 8>;
+
+enum GemmVariant { kVariantSingle = 0, kVariantPair256 = 1, kVariantPair128 = 2, kVariantPair192 = 3 };
+
+// Estimated relative cost of a variant: whole waves of tiles over the SMs (or
+// SM pairs), times the padded work one SM does per tile, divided by the
+// variant's measured tensor-pipe efficiency relative to the 1-SM 128x256 tile
+// (a pair stages half of B per SM; 256x128 pairs are slower than one SM,
+// see DESIGN.md, and are only used when forced).
+double variant_cost(int variant, int64_t rank, int64_t bm, int64_t bn, int sms) {
+  const bool pair = variant != kVariantSingle;
+  const int64_t tm = pair ? 256 : 128;
+  const int64_t tn = variant == kVariantPair128 ? 128 : (variant == kVariantPair192 ? 192 : 256);
+  const int64_t units = pair ? sms / 2 : sms;
+  const double efficiency = variant == kVariantSingle    ? 1.0
+                            : variant == kVariantPair256 ? 1.15
+                            : variant == kVariantPair192 ? 1.08
+                                                         : 0.70;
+  const int64_t tiles = rank * ceil_div(bm, tm) * ceil_div(bn, tn);
+  const int64_t waves = ceil_div(tiles, units);
+  return double(waves) * double(tm * tn / (pair ? 2 : 1)) / efficiency;
+}
+
+int choose_variant(int64_t rank, int64_t bm, int64_t bn, int sms) {
+  if (const char* forced = std::getenv("FMM_LEAF_GEMM_VARIANT")) {
+    const std::string v(forced);
+    if (v == "single") return kVariantSingle;
+    if (v == "pair256") return kVariantPair256;
+    if (v == "pair192") return kVariantPair192;
+    if (v == "pair128") return kVariantPair128;
+  }
+  int best = kVariantSingle;
+  double best_cost = variant_cost(kVariantSingle, rank, bm, bn, sms);
+  for (int v : {kVariantPair256, kVariantPair192}) {
+    const double c = variant_cost(v, rank, bm, bn, sms);
+    if (c < best_cost) {
+      best = v;
+      best_cost = c;
+    }
+  }
+  return best;
+}
+
+template <class Kernel>
+int ensure_smem_attribute(bool& done, Kernel kernel, size_t bytes) {
+  if (done) return FMM_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(leaf GEMM)");
+  done = true;
+  return FMM_OK;
+}
+
+template <class Cfg>
+int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_t ldk, int sms,
+                bool& configured, cudaStream_t stream) {
+  CUtensorMap map_l, map_r;
+  if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM)) return rc;
+  if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, Cfg::kBN / 2)) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (int rc = ensure_smem_attribute(configured, leaf_gemm_pair_kernel<Cfg>, Cfg::kSmemBytes)) return rc;
+  }
+  const int64_t tiles = int64_t(prm.rank) * ceil_div(prm.bm, Cfg::kTileM) * ceil_div(prm.bn, Cfg::kBN);
+  const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg>, map_l, map_r, prm);
+  if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM (pair) launch");
+  return FMM_OK;
+}
 
 int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
                      void* P, cudaStream_t stream) {
@@ -227,19 +324,6 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
   const int64_t ldk = round_up(bk, 8), ldp = round_up(bn, 8);
-  CUtensorMap map_l, map_r;
-  if (int rc = plane_map(&map_l, L, bk, bm, ldk, rank, kGemmBM)) return rc;
-  if (int rc = plane_map(&map_r, Rt, bk, bn, ldk, rank, GemmCfg::kBN)) return rc;
-  {
-    std::lock_guard<std::mutex> lock(g_device_mutex);
-    if (!info->gemm_configured) {
-      cudaError_t e = cudaFuncSetAttribute(leaf_gemm_kernel<GemmCfg>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(GemmCfg::kSmemBytes));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(leaf GEMM)");
-      info->gemm_configured = true;
-    }
-  }
   LeafGemmParams prm;
   prm.bm = bm;
   prm.bn = bn;
@@ -251,8 +335,25 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   prm.group_m = 16;
   prm.P = static_cast<__half*>(P);
   prm.timeout_ns = g_timeout_ns;
+  if (int64_t(rank) * ceil_div(bm, kGemmBM) * ceil_div(bn, 128) > (int64_t(1) << 30))
+    return fail(FMM_ERR_TOO_LARGE, "too many GEMM tiles");
+  const int variant = choose_variant(rank, bm, bn, info->sm_count);
+  if (variant == kVariantPair256)
+    return launch_pair<PairCfg256>(L, Rt, prm, ldk, info->sm_count, info->pair256_configured, stream);
+  if (variant == kVariantPair192)
+    return launch_pair<PairCfg192>(L, Rt, prm, ldk, info->sm_count, info->pair192_configured, stream);
+  if (variant == kVariantPair128)
+    return launch_pair<PairCfg128>(L, Rt, prm, ldk, info->sm_count, info->pair128_configured, stream);
+  CUtensorMap map_l, map_r;
+  if (int rc = plane_map(&map_l, L, bk, bm, ldk, rank, kGemmBM)) return rc;
+  if (int rc = plane_map(&map_r, Rt, bk, bn, ldk, rank, GemmCfg::kBN)) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (int rc = ensure_smem_attribute(info->gemm_configured, leaf_gemm_kernel<GemmCfg>,
+                                       GemmCfg::kSmemBytes))
+      return rc;
+  }
   const int64_t tiles = int64_t(rank) * prm.tiles_m * prm.tiles_n;
-  if (tiles > (int64_t(1) << 30)) return fail(FMM_ERR_TOO_LARGE, "too many GEMM tiles");
   const int grid = static_cast<int>(tiles < info->sm_count ? tiles : info->sm_count);
   leaf_gemm_kernel<GemmCfg><<<grid, kGemmThreads, GemmCfg::kSmemBytes, stream>>>(map_l, map_r, prm);
   cudaError_t e = cudaGetLastError();

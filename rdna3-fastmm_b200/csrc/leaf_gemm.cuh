@@ -271,4 +271,245 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs on a TPC computes one 256 x BN tile with
+// tcgen05.mma.cta_group::2 (M = 256).  CTA r of the pair holds rows
+// [128 r, 128 r + 128) of the L tile and rows [BN/2 r, BN/2 r + BN/2) of the
+// Rt tile in its own shared memory; the tensor cores of the pair read both
+// halves, so each SM stages half of the B operand it would need alone -- per
+// 64-deep stage 16 KiB of L and BN*64 B of Rt per SM, i.e. about 128 B/clk of
+// shared-memory traffic at the full MMA rate instead of 192.
+//
+// Roles (both CTAs unless noted):
+//   warp 0   TMA producer: waits on its own `empty` stage barrier (released by
+//            the pair's multicast commit), loads its halves; the bytes complete
+//            on the EVEN CTA's `full` barrier (.cta_group::2 TMA), where the even
+//            CTA's producer has posted the expected byte count of both halves.
+//   warp 1   TMEM allocation for the pair (both CTAs); in the even CTA one
+//            thread issues the MMAs and the multicast commits.
+//   warps 2-5 epilogue: each CTA drains its own 128 accumulator lanes and
+//            signals the even CTA's `tmem_empty` barrier (8 arrivals).
+// No TMA multicast is used: every CTA loads only its own halves.
+template <int BN, int STAGES>
+struct LeafGemmPairConfig {
+  static constexpr int kBN = BN;
+  static constexpr int kStages = STAGES;
+  static constexpr int kTileM = 2 * kGemmBM;                  // 256 rows per pair
+  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;   // this CTA's L half: 16 KiB
+  static constexpr uint32_t kBBytes = (BN / 2) * kGemmBK * 2;  // this CTA's Rt half
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  // two accumulators of BN columns; the allocation is a power of two
+  static constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256 : 512;
+  static constexpr size_t kSmemBytes = size_t(STAGES) * kStageBytes + 1024 + 256;
+  static_assert(2 * BN <= 512 && BN % 32 == 0, "two BN-column accumulators must fit in TMEM");
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
+
+template <class Cfg>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    leaf_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_l,
+                          const __grid_constant__ CUtensorMap tmap_r, const LeafGemmParams p) {
+  constexpr int BN = Cfg::kBN;
+  constexpr int STAGES = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t a_base = base;
+  const uint32_t b_base = base + STAGES * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes);
+  const uint32_t full_bar = smem_u32(bars);                     // [STAGES], used in CTA 0
+  const uint32_t empty_bar = smem_u32(bars + STAGES);           // [STAGES], each CTA
+  const uint32_t tfull_bar = smem_u32(bars + 2 * STAGES);       // [2], each CTA
+  const uint32_t tempty_bar = smem_u32(bars + 2 * STAGES + 2);  // [2], used in CTA 0
+  const uint32_t drain_bar = smem_u32(bars + 2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t cta = cluster_cta_rank();  // 0 = even CTA (issues the MMAs)
+  const int pair = blockIdx.x / 2;
+  const int pairs = gridDim.x / 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar + 8 * s, 1);
+      mbar_init(empty_bar + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar + 8 * b, 1);
+      mbar_init(tempty_bar + 8 * b, 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmap_l);
+    prefetch_tmap(&tmap_r);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_m = static_cast<int>((p.bm + Cfg::kTileM - 1) / Cfg::kTileM);
+  const int tiles_n = static_cast<int>((p.bn + BN - 1) / BN);
+  LeafGemmParams q = p;
+  q.tiles_m = tiles_m;
+  q.tiles_n = tiles_n;
+  const int total_tiles = p.rank * tiles_m * tiles_n;
+  const int k_blocks = static_cast<int>((p.bk + kGemmBK - 1) / kGemmBK);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producers
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int issued = 0;
+      for (int t = pair; t < total_tiles && ok; t += pairs) {
+        int r, tm, tn;
+        leaf_tile_coords(q, t, r, tm, tn);
+        const int a_row = tm * Cfg::kTileM + static_cast<int>(cta) * kGemmBM;
+        const int b_row = tn * BN + static_cast<int>(cta) * (BN / 2);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait_bounded_cluster(empty_bar + 8 * stage, phase ^ 1u, abort, p.timeout_ns, 11)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_even = map_to_cta(full_bar + 8 * stage, 0);
+          if (cta == 0) mbar_arrive_expect_tx(full_bar + 8 * stage, 2 * Cfg::kStageBytes);
+          tma_load_3d_pair(a_base + stage * Cfg::kABytes, &tmap_l, full_even, kb * kGemmBK, a_row, r);
+          tma_load_3d_pair(b_base + stage * Cfg::kBBytes, &tmap_r, full_even, kb * kGemmBK, b_row, r);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && issued > 0) {
+        // loads may still be landing in this CTA's shared memory: give them
+        // time to finish (they complete on the even CTA's barrier, which this
+        // CTA cannot wait on) before the CTA unwinds
+        const uint64_t start = globaltimer_ns();
+        while (globaltimer_ns() - start < 200000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (cta == 0 && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(Cfg::kTileM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = pair; t < total_tiles && ok; t += pairs) {
+        if (!mbar_wait_bounded_cluster(tempty_bar + 8 * acc, acc_phase ^ 1u, abort, p.timeout_ns, 12)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait_bounded_cluster(full_bar + 8 * stage, phase, abort, p.timeout_ns, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = a_base + stage * Cfg::kABytes;
+          const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            tc_mma_f16_pair(d_tmem, smem_desc_k_sw128(a_addr + kk * 32),
+                            smem_desc_k_sw128(b_addr + kk * 32), idesc,
+                            (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          tc_commit_pair_multicast(empty_bar + 8 * stage, 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_multicast(tfull_bar + 8 * acc, 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued_any) {
+        tc_commit_pair_multicast(drain_bar, 0x1);
+        volatile int no_abort = 0;
+        mbar_wait_bounded(drain_bar, 0, &no_abort, p.timeout_ns, 16);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row_in_tile = static_cast<int>(cta) * kGemmBM + quarter * 32 + lane;
+    const uint32_t tempty_even = map_to_cta(tempty_bar, 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < total_tiles; t += pairs) {
+      int r, tm, tn;
+      leaf_tile_coords(q, t, r, tm, tn);
+      int ready = 0;
+      if (lane == 0)
+        ready = mbar_wait_bounded_cluster(tfull_bar + 8 * acc, acc_phase, abort, p.timeout_ns, 14) ? 1 : 0;
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * Cfg::kTileM + row_in_tile;
+      __half* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
+      const uint32_t t_addr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tc_ld_32x32b_x32(t_addr + c, v);
+        tc_wait_ld();
+        const int64_t col = static_cast<int64_t>(tn) * BN + c;
+        if (row < p.bm) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int64_t c8 = col + g * 8;
+            if (c8 + 8 <= p.ldp) {
+              uint4 pk;
+              __half2* h = reinterpret_cast<__half2*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                h[e] = __floats2half2_rn(__uint_as_float(v[g * 8 + 2 * e]),
+                                         __uint_as_float(v[g * 8 + 2 * e + 1]));
+              *reinterpret_cast<uint4*>(prow + c8) = pk;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty_even + 8 * acc);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // nobody leaves while the pair may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+}
+
 }  // namespace fmm

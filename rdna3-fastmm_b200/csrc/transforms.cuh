@@ -54,6 +54,11 @@ template <int N>
 struct VecIO;
 
 template <>
+struct VecIO<2> {
+  using BF = unsigned int;  // 2 x bf16
+  using H = unsigned int;   // 2 x fp16
+};
+template <>
 struct VecIO<4> {
   using BF = uint2;   // 4 x bf16
   using H = uint2;    // 4 x fp16
@@ -65,8 +70,7 @@ struct VecIO<8> {
 };
 
 template <int N>
-__device__ __forceinline__ VecF<N> load_bf16_vec(const __nv_bfloat16* p) {
-  typename VecIO<N>::BF raw = __ldg(reinterpret_cast<const typename VecIO<N>::BF*>(p));
+__device__ __forceinline__ VecF<N> unpack_bf16(const typename VecIO<N>::BF& raw) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
   VecF<N> r;
 #pragma unroll
@@ -79,8 +83,7 @@ __device__ __forceinline__ VecF<N> load_bf16_vec(const __nv_bfloat16* p) {
 }
 
 template <int N>
-__device__ __forceinline__ VecF<N> load_half_vec(const __half* p) {
-  typename VecIO<N>::H raw = *reinterpret_cast<const typename VecIO<N>::H*>(p);
+__device__ __forceinline__ VecF<N> unpack_half(const typename VecIO<N>::H& raw) {
   const __half2* h = reinterpret_cast<const __half2*>(&raw);
   VecF<N> r;
 #pragma unroll
@@ -124,12 +127,17 @@ __device__ __forceinline__ void store_bf16_vec(__nv_bfloat16* p, const VecF<N>& 
 //
 // Thread mapping: one thread per VEC consecutive plane columns of one plane
 // row; consecutive threads take consecutive vectors, so every block load and
-// plane store of a warp is one contiguous span.  Columns in [bcols, ldd) are
-// padding and are written as zeros.
-template <class Prog, int S, int VEC, bool kWeight>
-__global__ void __launch_bounds__(256) block_transform_kernel(
+// plane store of a warp is one contiguous span.  All S*S source vectors are
+// loaded (packed, 2 bytes per element) before any arithmetic, so each thread
+// has every load in flight at once; the generated program then unpacks them
+// as it needs them.  This memory-level parallelism is what keeps the rank-48/49
+// transforms near HBM bandwidth.  Columns in [bcols, ldd) are padding and are
+// written as zeros.
+template <class Prog, int S, int VEC, bool kWeight, int THREADS = 256, int MIN_BLOCKS = 1>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
     const __nv_bfloat16* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
     __half* __restrict__ dst, int64_t brows, int64_t bcols, int64_t ldd, int vector_loads) {
+  using Raw = typename VecIO<VEC>::BF;
   const int64_t plane = brows * ldd;
   const uint32_t vecs_per_row = static_cast<uint32_t>(ldd / VEC);
   const uint32_t total = static_cast<uint32_t>(brows) * vecs_per_row;
@@ -137,23 +145,35 @@ __global__ void __launch_bounds__(256) block_transform_kernel(
        idx += gridDim.x * blockDim.x) {
     const uint32_t i = idx / vecs_per_row;
     const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
-    auto in = [&](int q) -> VecF<VEC> {
-      const int br = kWeight ? (q % S) : (q / S);
-      const int bc = kWeight ? (q / S) : (q % S);
-      const int64_t r = br * brows + i;
-      const int64_t c0 = bc * bcols + j;
-      VecF<VEC> x;
-      if (vector_loads && r < rows && j + VEC <= bcols && c0 + VEC <= cols) {
-        x = load_bf16_vec<VEC>(src + r * ld + c0);
-      } else {
+    Raw raw[Prog::kInputs];
+    // interior vectors (every source block in range, aligned source): one
+    // test per thread, then S*S unconditional vector loads back to back
+    const bool interior = vector_loads && (S - 1) * brows + i < rows && j + VEC <= bcols &&
+                          (S - 1) * bcols + j + VEC <= cols;
+    if (interior) {
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          const bool ok = r < rows && j + e < bcols && c0 + e < cols;
-          x.v[e] = ok ? __bfloat162float(src[r * ld + c0 + e]) : 0.0f;
+      for (int q = 0; q < Prog::kInputs; ++q) {
+        const int br = kWeight ? (q % S) : (q / S);
+        const int bc = kWeight ? (q / S) : (q % S);
+        raw[q] = __ldg(reinterpret_cast<const Raw*>(src + (br * brows + i) * ld + bc * bcols + j));
+      }
+    } else {
+      // ragged edge or unaligned source: element loads with zero padding
+#pragma unroll
+      for (int q = 0; q < Prog::kInputs; ++q) {
+        const int br = kWeight ? (q % S) : (q / S);
+        const int bc = kWeight ? (q / S) : (q % S);
+        const int64_t r = br * brows + i;
+        const int64_t c0 = bc * bcols + j;
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw[q]);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          const bool ok = r < rows && j + k < bcols && c0 + k < cols;
+          e[k] = ok ? src[r * ld + c0 + k] : __float2bfloat16(0.0f);
         }
       }
-      return x;
-    };
+    }
+    auto in = [&](int q) -> VecF<VEC> { return unpack_bf16<VEC>(raw[q]); };
     auto out = [&](int o, const VecF<VEC>& x) {
       store_half_vec<VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
     };
@@ -164,12 +184,14 @@ __global__ void __launch_bounds__(256) block_transform_kernel(
 // ---------------------------------------------------------------------------
 // Output side (unfused reconstruct): P[r][bm][ldp] FP16 -> C[M,N] BF16.
 // Output o is C block (o / S, o % S); bias[bc*bn + c] is added after the whole
-// recombination, then rounded to nearest even BF16.
-template <class Prog, int S, int VEC>
-__global__ void __launch_bounds__(256) reconstruct_kernel(
+// recombination, then rounded to nearest even BF16.  As in the input side, all
+// R product vectors are loaded before the arithmetic.
+template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
     const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
     const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ C, int64_t M, int64_t N,
     int64_t ldc, int vector_stores) {
+  using Raw = typename VecIO<VEC>::H;
   const int64_t plane = bm * ldp;
   const uint32_t vecs_per_row = static_cast<uint32_t>((bn + VEC - 1) / VEC);
   const uint32_t total = static_cast<uint32_t>(bm) * vecs_per_row;
@@ -177,9 +199,11 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(
        idx += gridDim.x * blockDim.x) {
     const uint32_t i = idx / vecs_per_row;
     const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
-    auto in = [&](int r) -> VecF<VEC> {
-      return load_half_vec<VEC>(P + r * plane + static_cast<int64_t>(i) * ldp + j);
-    };
+    Raw raw[Prog::kInputs];
+#pragma unroll
+    for (int r = 0; r < Prog::kInputs; ++r)
+      raw[r] = __ldg(reinterpret_cast<const Raw*>(P + r * plane + static_cast<int64_t>(i) * ldp + j));
+    auto in = [&](int r) -> VecF<VEC> { return unpack_half<VEC>(raw[r]); };
     auto out = [&](int o, const VecF<VEC>& x) {
       const int br = o / S, bc = o % S;
       const int64_t row = br * bm + i;

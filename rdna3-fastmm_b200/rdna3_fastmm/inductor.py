@@ -33,7 +33,9 @@ def _enable_external_matmul() -> bool:
 
 def compile_backend(graph_module: GraphModule, example_inputs: Sequence[torch.Tensor], *,
                     mode: str | None = None, options: dict[str, Any] | None = None) -> CompiledGraph:
-    inductor_options = torch._inductor.list_mode_options(mode)
+    # ``list_mode_options(None)`` returns the table of every mode, not the
+    # default mode's options; resolve None to "default" first
+    inductor_options = dict(torch._inductor.list_mode_options(mode or "default"))
     inductor_options.update(options or {})
     if _enable_external_matmul():
         rewrite_eligible_linears(graph_module, list(example_inputs))

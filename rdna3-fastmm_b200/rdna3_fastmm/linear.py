@@ -23,6 +23,7 @@ from typing import Callable, Optional
 
 import torch
 from torch.fx import GraphModule, Node
+from torch._subclasses.fake_tensor import FakeTensorMode
 from torch.fx.passes.fake_tensor_prop import FakeTensorProp
 
 from . import _native
@@ -165,7 +166,9 @@ def rewrite_eligible_linears(graph_module: GraphModule, example_inputs: list[tor
     nodes = tuple(n for n in graph_module.graph.nodes
                   if n.op == "call_function" and n.target in LINEAR_TARGETS)
     if any(isinstance(a, Node) and _node_tensor(a) is None for n in nodes for a in n.args):
-        FakeTensorProp(graph_module).propagate(*example_inputs)
+        # parameters reached through get_attr are real tensors; let the fake
+        # mode wrap them instead of refusing the graph
+        FakeTensorProp(graph_module, FakeTensorMode(allow_non_fake_inputs=True)).propagate(*example_inputs)
     rewritten = 0
     for node in nodes:
         target = _linear_node_target(node)

@@ -88,11 +88,15 @@ def test_reconstruct_matches_oracle_bitwise(name, shape, with_bias):
     np.testing.assert_array_equal(_bits(C), oracle.bf16_bits(ref).view(np.int16))
 
 
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair128"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
-    [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (2, 129, 257, 1000), (48, 64, 72, 130)],
+    [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (2, 129, 257, 1000), (48, 64, 72, 130),
+     (5, 700, 900, 520)],
 )
-def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk):
+def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch):
+    """Every leaf-GEMM kernel (1-SM 128x256, 2-SM 256x256, 2-SM 256x128)."""
+    monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
     g = torch.Generator().manual_seed(rank * 1000 + bm)
     ldk = -(-bk // 8) * 8
     ldp = -(-bn // 8) * 8

@@ -60,3 +60,25 @@ def test_cpu_linears_are_not_rewritten():
     model = torch.nn.Sequential(torch.nn.Linear(8, 8), torch.nn.ReLU()).to(torch.bfloat16)
     gm = torch.fx.symbolic_trace(model)
     assert linear.rewrite_eligible_linears(gm, [torch.randn(4, 8, dtype=torch.bfloat16)]) == 0
+
+
+def test_pyproject_registers_named_dynamo_backend():
+    import tomllib
+    from pathlib import Path
+
+    pyproject = tomllib.loads((Path(__file__).resolve().parent.parent / "pyproject.toml").read_text())
+    assert pyproject["project"]["entry-points"]["torch_dynamo_backends"] == {
+        "rdna3-fastmm": "rdna3_fastmm.inductor:compile_backend"
+    }
+
+
+def test_default_mode_resolves_to_default_options(monkeypatch):
+    captured = {}
+    monkeypatch.setattr(torch._inductor, "compile",
+                        lambda gm, inputs, options: captured.__setitem__("options", options))
+    monkeypatch.setattr(inductor, "_enable_external_matmul", lambda: False)
+    gm = torch.fx.symbolic_trace(lambda v: v.cos())
+    inductor.compile_backend(gm, [torch.randn(4)])
+    assert captured["options"] == {}
+    inductor.compile_backend(gm, [torch.randn(4)], mode="reduce-overhead")
+    assert captured["options"] == {"triton.cudagraphs": True}
