@@ -192,11 +192,11 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         description += f" (rows overridden to {M_total})"
     shard = args.shard and world > 1
     if shard:
-        from rdna3_fastmm.distributed import shard_rows
-
-        row_start, M = shard_rows(M_total, world)[rank]
-        padded = -(-M_total // world)
-        description += f"; rows sharded over {world} GPUs, output all-gathered (NCCL)"
+        if M_total % (world * args.chunks):
+            raise SystemExit("--shard needs M divisible by gpus * chunks")
+        M = M_total // world
+        description += (f"; rows sharded block-cyclically over {world} GPUs in {args.chunks} chunks, "
+                        f"output all-gathered (NCCL) chunk by chunk, overlapped with compute")
     else:
         M = M_total
     plan = plans[scheme](M, K, N, device, dtype=torch.bfloat16, compute_dtype=torch.float16)
@@ -209,12 +209,7 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     ws = plan.allocate_workspace(0.9, prepacked_right=prepacked)
     packed = plan.pack_weight(W, 0.9) if prepacked else None
     right = packed.transformed if prepacked else ws.right_transformed
-    if shard:
-        gathered = torch.empty((world * padded, N), device=device, dtype=torch.bfloat16)
-        slot = gathered[rank * padded:(rank + 1) * padded]
-        out = slot[:M]
-    else:
-        out = torch.empty((M, N), device=device, dtype=torch.bfloat16)
+    out = torch.empty((M, N), device=device, dtype=torch.bfloat16)
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
     s = plan.shape
     stream = torch.cuda.current_stream(device)
@@ -231,8 +226,6 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         ev[3].record(stream)
         _native.reconstruct(scheme, ws.products, M, N, bias, out)
         ev[4].record(stream)
-        if shard:
-            dist.all_gather_into_tensor(gathered, slot)
         ev[5].record(stream)
 
     def barrier():
@@ -262,14 +255,38 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         stages["all_gather"].append(ev[4].elapsed_time(ev[5]))
         totals.append(ev[0].elapsed_time(ev[5]))
     total_ms = sum(totals)
+    if shard:
+        from rdna3_fastmm.distributed import RowShardedLinear
+
+        layer = RowShardedLinear(plans[scheme], M_total, W, bias=bias, chunks=args.chunks,
+                                 reserve_sms=args.reserve_sms, max_free_memory_fraction=0.9)
+        gathered = layer.gather_buffer()
+        for _ in range(args.warmup):
+            flush.zero_()
+            layer(A, out=gathered)
+        torch.cuda.synchronize(device)
+        barrier()
+        shard_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                        for _ in range(args.steps)]
+        with ClockSampler(device.index) as shard_clocks:
+            for e0, e1 in shard_events:
+                flush.zero_()
+                e0.record(stream)
+                layer(A, out=gathered)
+                e1.record(stream)
+            torch.cuda.synchronize(device)
+            barrier()
+        compute_ms = total_ms
+        total_ms = sum(a.elapsed_time(b) for a, b in shard_events)
+        clocks = shard_clocks
     status, _ = _native.device_status(device.index)
     if status:
         raise RuntimeError(f"device status {status:#x} after the timed region")
     if args.profile:
         if rank == 0:
-            print(json.dumps({"profile_run": args.workload, "M": M, "K": K, "N": N,
-                              "ms_per_step": total_ms / args.steps,
-                              "stages_ms": {k: statistics.mean(v) for k, v in stages.items()}}))
+            _emit({"profile_run": args.workload, "M": M, "K": K, "N": N,
+                   "ms_per_step": total_ms / args.steps,
+                   "stages_ms": {k: statistics.mean(v) for k, v in stages.items()}})
         return None
 
     # parity spot check of this very output against the FP64 product (sampled rows)
@@ -304,10 +321,7 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     b_d = torch.empty_like(bias) if bias is not None else None
 
     if shard:
-        from rdna3_fastmm.distributed import RowShardedLinear
-
-        layer = RowShardedLinear(plans[scheme], M_total, W, bias=bias, max_free_memory_fraction=0.9)
-        C_pin = torch.empty((world * padded, N), dtype=torch.bfloat16).pin_memory()
+        C_pin = torch.empty(tuple(gathered.shape), dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
         A_d.copy_(A_pin, non_blocking=True)
@@ -375,10 +389,10 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         "reconstruct": hbm(r_bytes, statistics.mean(stages["reconstruct"])),
     }
     if shard:
-        gather_ms = statistics.mean(stages["all_gather"])
-        moved = (world - 1) * padded * N * 2  # bytes each rank receives
-        kernels["all_gather"] = {"ms": round(gather_ms, 4), "bytes_received": moved,
-                                 "gbs": round(moved / (gather_ms * 1e-3) / 1e9, 1) if gather_ms > 0 else None}
+        moved = (world - 1) * M * N * 2  # bytes each rank receives
+        kernels["sharded_step"] = {"ms": round(ms_per_step, 4), "compute_only_ms": round(compute_ms / args.steps, 4),
+                                   "gather_bytes_received": moved, "chunks": args.chunks,
+                                   "nvlink_gbs_if_gather_bound": round(moved / (ms_per_step * 1e-3) / 1e9, 1)}
     traffic = profile_traffic(args.workload)
     line = {
         "metric": "effective TFLOP/s (2MNK/t) per B200 and at 8 GPUs; speedup vs cuBLAS BF16",
@@ -418,7 +432,20 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     return line
 
 
+def _emit(line: dict) -> None:
+    os.write(_JSON_FD, (json.dumps(line) + "\n").encode())
+
+
+_JSON_FD = 1
+
+
 def main() -> None:
+    global _JSON_FD
+    # libraries (NCCL's version banner, for one) may write to stdout; keep
+    # the real stdout for the single JSON line and send everything else to stderr
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=100)
@@ -430,6 +457,10 @@ def main() -> None:
                         help="override M (smaller cases for profiler captures)")
     parser.add_argument("--shard", action="store_true",
                         help="split M over the ranks and all-gather C (strong scaling)")
+    parser.add_argument("--chunks", type=int, default=4,
+                        help="row chunks per rank in --shard mode (gather overlaps compute)")
+    parser.add_argument("--reserve-sms", type=int, default=32,
+                        help="SMs left free for NCCL while --shard chunks compute")
     parser.add_argument("--profile", action="store_true",
                         help="timed steps only: no cuBLAS, e2e, parity or CPU legs")
     args = parser.parse_args()
@@ -448,7 +479,7 @@ def main() -> None:
         value = statistics.median(s["value"] for s in samples)
         base = dict(samples[0])
         base["value"] = value
-        print(json.dumps({
+        _emit({
             "impl": "reference",
             "metric": "effective TFLOP/s (2MNK/t) per B200 and at 8 GPUs; speedup vs cuBLAS BF16",
             "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -458,7 +489,7 @@ def main() -> None:
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-        }), flush=True)
+        })
         return
 
     import torch
@@ -476,7 +507,7 @@ def main() -> None:
             if not args.no_cpu_baseline:
                 cpu = cpu_sample(args.workload)
                 line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
-            print(json.dumps(line), flush=True)
+            _emit(line)
     finally:
         if world > 1:
             dist.destroy_process_group()

@@ -133,6 +133,13 @@ int fmm_linear(int scheme, const void* A, const void* W, const void* bias, void*
 int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bias, void* C,
                        int64_t M, int64_t K, int64_t N, fmm_stream_t stream);
 
+/* Most SMs any later launch of this library may fill (0 = all, the default;
+ * odd values round down to even).  Leaving SMs free lets work on other
+ * streams -- an NCCL all-gather of finished output rows, for instance -- run
+ * alongside the persistent leaf GEMM.  Process-wide.  No counterpart in the
+ * reference. */
+int fmm_set_sm_budget(int sms);
+
 /* Upper bound, in nanoseconds, of every device-side wait (default 2 s).  A
  * wait that runs out records FMM_STATUS_TIMEOUT and unwinds the kernel.  No
  * counterpart in the reference (it has no device-side waits). */

@@ -29,6 +29,7 @@ namespace {
 
 thread_local std::string t_last_error;
 uint64_t g_timeout_ns = 2000000000ull;  // 2 s per wait
+int g_sm_budget = 0;                     // 0: every SM; else the most SMs one launch may fill
 
 int fail(int code, const std::string& what) {
   t_last_error = what;
@@ -112,6 +113,14 @@ int device_info(DeviceInfo** out) {
   return FMM_OK;
 }
 
+// SMs a launch may fill: all of them, or the budget set by fmm_set_sm_budget
+// (kept even so that SM pairs of the 2-SM GEMM stay whole).
+int usable_sms(const DeviceInfo* info) {
+  int sms = info->sm_count;
+  if (g_sm_budget > 0 && g_sm_budget < sms) sms = g_sm_budget & ~1;
+  return sms < 2 ? 2 : sms;
+}
+
 // ------------------------------------------------------------------ dispatch
 // Launch shapes were swept on B200 with random data (threads per block,
 // minimum resident blocks, grid cap in blocks per SM); with every input
@@ -151,7 +160,7 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
 
 int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int blocks_per_sm) {
   const int64_t blocks = ceil_div(work_items, threads);
-  const int64_t cap = int64_t(info->sm_count) * blocks_per_sm;
+  const int64_t cap = int64_t(usable_sms(info)) * blocks_per_sm;
   return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 
@@ -337,13 +346,14 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   prm.timeout_ns = g_timeout_ns;
   if (int64_t(rank) * ceil_div(bm, kGemmBM) * ceil_div(bn, 128) > (int64_t(1) << 30))
     return fail(FMM_ERR_TOO_LARGE, "too many GEMM tiles");
-  const int variant = choose_variant(rank, bm, bn, info->sm_count);
+  const int sms = usable_sms(info);
+  const int variant = choose_variant(rank, bm, bn, sms);
   if (variant == kVariantPair256)
-    return launch_pair<PairCfg256>(L, Rt, prm, ldk, info->sm_count, info->pair256_configured, stream);
+    return launch_pair<PairCfg256>(L, Rt, prm, ldk, sms, info->pair256_configured, stream);
   if (variant == kVariantPair192)
-    return launch_pair<PairCfg192>(L, Rt, prm, ldk, info->sm_count, info->pair192_configured, stream);
+    return launch_pair<PairCfg192>(L, Rt, prm, ldk, sms, info->pair192_configured, stream);
   if (variant == kVariantPair128)
-    return launch_pair<PairCfg128>(L, Rt, prm, ldk, info->sm_count, info->pair128_configured, stream);
+    return launch_pair<PairCfg128>(L, Rt, prm, ldk, sms, info->pair128_configured, stream);
   CUtensorMap map_l, map_r;
   if (int rc = plane_map(&map_l, L, bk, bm, ldk, rank, kGemmBM)) return rc;
   if (int rc = plane_map(&map_r, Rt, bk, bn, ldk, rank, GemmCfg::kBN)) return rc;
@@ -354,7 +364,7 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
       return rc;
   }
   const int64_t tiles = int64_t(rank) * prm.tiles_m * prm.tiles_n;
-  const int grid = static_cast<int>(tiles < info->sm_count ? tiles : info->sm_count);
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   leaf_gemm_kernel<GemmCfg><<<grid, kGemmThreads, GemmCfg::kSmemBytes, stream>>>(map_l, map_r, prm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM launch");
@@ -508,6 +518,12 @@ int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bia
   // in the same call (pitch padding included), so nothing is cleared first.
   return fmm_linear(scheme, A, W, bias, C, M, K, N, bytes, bytes + left, bytes + left + right, 0u,
                     stream);
+}
+
+int fmm_set_sm_budget(int sms) {
+  if (sms < 0) return fail(FMM_ERR_INVALID_ARGUMENT, "SM budget must be >= 0");
+  g_sm_budget = sms;
+  return FMM_OK;
 }
 
 int fmm_set_wait_timeout_ns(uint64_t timeout_ns) {

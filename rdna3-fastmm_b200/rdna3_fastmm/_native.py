@@ -60,6 +60,7 @@ _SIGNATURES = {
         ctypes.c_int,
     ),
     "fmm_linear_noalloc": ([ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P], ctypes.c_int),
+    "fmm_set_sm_budget": ([ctypes.c_int], ctypes.c_int),
     "fmm_set_wait_timeout_ns": ([ctypes.c_uint64], ctypes.c_int),
     "fmm_device_status": (
         [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32), ctypes.c_int],
@@ -153,6 +154,11 @@ def linear_noalloc(scheme: str, A, W, bias, C) -> int:
     N = C.shape[1]
     return library().fmm_linear_noalloc(SCHEME_IDS[scheme], _ptr(A), _ptr(W), _ptr(bias), _ptr(C),
                                         M, K, N, _stream(A.device))
+
+
+def set_sm_budget(sms: int) -> None:
+    """Cap the SMs one launch may fill (0 = all); see fmm_set_sm_budget."""
+    check(library().fmm_set_sm_budget(sms), "fmm_set_sm_budget")
 
 
 def set_wait_timeout_ns(timeout_ns: int) -> None:

@@ -8,13 +8,19 @@ blocks are all-gathered over NCCL (NVLink / NVSwitch).  Each rank writes its
 rows straight into its slot of the gather buffer and the all-gather runs in
 place, so no extra copy is made.
 
+With ``chunks > 1`` the rows are dealt out block-cyclically: chunk ``c`` of
+rank ``r`` is global row block ``c * world + r`` (``M / (world * chunks)`` rows
+each), so chunk ``c`` of every rank forms one contiguous slice of ``C``.  Each
+chunk is computed on the current stream and its slice is all-gathered
+asynchronously while the next chunk computes, overlapping NVLink traffic with
+tensor-core work.
+
 The reference is single-GPU; this is the multi-GPU form north_star asks for
 (M sharded across 1/2/4/8 GPUs, weight replicated, all-gather on demand).
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
@@ -37,24 +43,18 @@ def shard_rows(rows: int, world: int) -> list[tuple[int, int]]:
     return out
 
 
-@dataclass
-class _Shard:
-    start: int
-    count: int
-    padded: int  # rows of every slot in the gather buffer
-
-
 class RowShardedLinear:
     """``C = A @ weight^T (+ bias)`` with rows of ``A`` split over a process group.
 
     ``plan_type`` is one of the rank plans; ``weight`` is the full native
-    ``[N, K]`` weight, replicated on every rank and packed locally.  ``local_linear``
-    replaces the B200 plan for host-logic tests (it receives the local rows and
-    must return ``[count, N]``).
+    ``[N, K]`` weight, replicated on every rank and packed locally.  ``chunks``
+    (> 1 needs ``rows % (world * chunks) == 0``) overlaps the all-gather with
+    compute as described in the module docstring.  ``local_linear`` replaces
+    the B200 plan for host-logic tests: it receives ``(rows [n, K], out [n, N])``.
     """
 
     def __init__(self, plan_type, rows: int, weight: torch.Tensor, *, group=None,
-                 bias: Optional[torch.Tensor] = None,
+                 bias: Optional[torch.Tensor] = None, chunks: int = 1, reserve_sms: int = 0,
                  local_linear: Optional[Callable[[torch.Tensor, torch.Tensor], None]] = None,
                  max_free_memory_fraction: float = 0.75) -> None:
         self.group = group
@@ -62,15 +62,29 @@ class RowShardedLinear:
         self.rank = dist.get_rank(group)
         self.columns, self.inner = weight.shape
         self.rows = rows
-        start, count = shard_rows(rows, self.world)[self.rank]
-        self.shard = _Shard(start, count, -(-rows // self.world))
+        if chunks < 1:
+            raise ValueError("chunks must be positive")
+        if chunks > 1 and rows % (self.world * chunks):
+            raise ValueError("chunked sharding needs rows divisible by world * chunks")
+        self.chunks = chunks
+        if chunks > 1:
+            self.chunk_rows = rows // (self.world * chunks)
+            self.count = self.chunk_rows * chunks
+            self.padded = self.count
+        else:
+            start, self.count = shard_rows(rows, self.world)[self.rank]
+            self.start = start
+            self.chunk_rows = self.count
+            self.padded = -(-rows // self.world)
         self.bias = bias
         self.device = weight.device
+        # SMs left to NCCL while chunks compute (0: the library fills them all)
+        self.reserve_sms = reserve_sms
         if local_linear is not None:
             self._local = local_linear
             self.plan = None
         else:
-            self.plan = plan_type(count, self.inner, self.columns, weight.device,
+            self.plan = plan_type(self.chunk_rows, self.inner, self.columns, weight.device,
                                   dtype=weight.dtype, compute_dtype=torch.float16)
             self.packed = self.plan.pack_weight(weight, max_free_memory_fraction)
             self.workspace = self.plan.allocate_workspace(max_free_memory_fraction, prepacked_right=True)
@@ -79,37 +93,78 @@ class RowShardedLinear:
     def _plan_linear(self, local_rows: torch.Tensor, out: torch.Tensor) -> None:
         self.plan.run_linear_packed(local_rows, self.packed, self.workspace, self.bias, out)
 
+    def _reserve(self) -> bool:
+        if self.reserve_sms <= 0 or self.plan is None:
+            return False
+        from . import _native
+
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        _native.set_sm_budget(max(2, sms - self.reserve_sms))
+        return True
+
+    def _release(self, reserved: bool) -> None:
+        if reserved:
+            from . import _native
+
+            _native.set_sm_budget(0)
+
+    def row_blocks(self) -> list[tuple[int, int]]:
+        """(start, count) of the global rows this rank owns, in local order."""
+        if self.chunks == 1:
+            return [(self.start, self.count)]
+        ch = self.chunk_rows
+        return [((c * self.world + self.rank) * ch, ch) for c in range(self.chunks)]
+
     def local_rows(self, full: torch.Tensor) -> torch.Tensor:
-        """This rank's rows of a full ``[M, K]`` input (a view)."""
-        return full[self.shard.start:self.shard.start + self.shard.count]
+        """This rank's rows of a full ``[M, K]`` input (contiguous)."""
+        blocks = [full[s:s + n] for s, n in self.row_blocks()]
+        return blocks[0] if len(blocks) == 1 else torch.cat(blocks)
 
     def gather_buffer(self) -> torch.Tensor:
-        return torch.empty((self.world * self.shard.padded, self.columns), device=self.device,
+        return torch.empty((self.world * self.padded, self.columns), device=self.device,
                            dtype=torch.bfloat16)
 
     def __call__(self, local_rows: torch.Tensor, *, gather: bool = True,
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Run this rank's rows; with ``gather`` return the whole ``C[M, N]``
-        on every rank, else this rank's ``[count, N]`` rows."""
-        if tuple(local_rows.shape) != (self.shard.count, self.inner):
+        on every rank, else this rank's ``[count, N]`` rows (local order)."""
+        if tuple(local_rows.shape) != (self.count, self.inner):
             raise ValueError(f"local rows have shape {tuple(local_rows.shape)}, "
-                             f"expected {(self.shard.count, self.inner)}")
+                             f"expected {(self.count, self.inner)}")
+        ch = self.chunk_rows
         if not gather:
             result = out if out is not None else torch.empty(
-                (self.shard.count, self.columns), device=self.device, dtype=torch.bfloat16)
-            self._local(local_rows, result)
+                (self.count, self.columns), device=self.device, dtype=torch.bfloat16)
+            for c in range(self.chunks):
+                self._local(local_rows[c * ch:(c + 1) * ch], result[c * ch:(c + 1) * ch])
             return result
         full = out if out is not None else self.gather_buffer()
-        if tuple(full.shape) != (self.world * self.shard.padded, self.columns):
+        if tuple(full.shape) != (self.world * self.padded, self.columns):
             raise ValueError("gather buffer does not match the sharding")
-        slot = full[self.rank * self.shard.padded:(self.rank + 1) * self.shard.padded]
-        self._local(local_rows, slot[: self.shard.count])
-        if self.shard.count < self.shard.padded:
-            slot[self.shard.count:].zero_()
+        if self.chunks > 1:
+            handles = []
+            span = self.world * ch
+            budget = self._reserve()
+            try:
+                for c in range(self.chunks):
+                    region = full[c * span:(c + 1) * span]
+                    slot = region[self.rank * ch:(self.rank + 1) * ch]
+                    self._local(local_rows[c * ch:(c + 1) * ch], slot)
+                    handles.append(dist.all_gather_into_tensor(region, slot, group=self.group,
+                                                               async_op=True))
+            finally:
+                self._release(budget)
+            for handle in handles:
+                handle.wait()
+            return full
+        slot = full[self.rank * self.padded:(self.rank + 1) * self.padded]
+        self._local(local_rows, slot[: self.count])
+        if self.count < self.padded:
+            slot[self.count:].zero_()
         dist.all_gather_into_tensor(full, slot, group=self.group)
-        if self.rows == self.world * self.shard.padded:
+        if self.rows == self.world * self.padded:
             return full
         # uneven split: drop the padding rows of the short slots
-        pieces = [full[r * self.shard.padded:r * self.shard.padded + c]
+        pieces = [full[r * self.padded:r * self.padded + c]
                   for r, (_, c) in enumerate(shard_rows(self.rows, self.world))]
         return torch.cat(pieces)

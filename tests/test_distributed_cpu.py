@@ -29,7 +29,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, rows, mode, results):
+def _worker(rank, world, port, rows, mode, results, chunks=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
@@ -41,15 +41,15 @@ def _worker(rank, world, port, rows, mode, results):
         def local(x, out):
             out.copy_(torch.nn.functional.linear(x, W))
 
-        layer = RowShardedLinear(None, rows, W, local_linear=local)
+        layer = RowShardedLinear(None, rows, W, local_linear=local, chunks=chunks)
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 leaves before the collective")
         try:
             full = layer(layer.local_rows(A))
             mine = layer(layer.local_rows(A), gather=False)
             expected = torch.nn.functional.linear(A, W)
-            results[rank] = bool(torch.equal(full, expected)) and bool(
-                torch.equal(mine, expected[layer.shard.start:layer.shard.start + layer.shard.count]))
+            mine_expected = torch.cat([expected[s:s + n] for s, n in layer.row_blocks()])
+            results[rank] = bool(torch.equal(full, expected)) and bool(torch.equal(mine, mine_expected))
         except RuntimeError as error:  # the peer is gone: the collective errors out
             results[rank] = f"error: {type(error).__name__}"
     except RuntimeError:
@@ -61,11 +61,12 @@ def _worker(rank, world, port, rows, mode, results):
             pass
 
 
-def _run(world, rows, mode):
+def _run(world, rows, mode, chunks=1):
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, rows, mode, results)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, rows, mode, results, chunks))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -77,6 +78,12 @@ def _run(world, rows, mode):
 @pytest.mark.parametrize("rows", [64, 37])
 def test_two_rank_gather_matches_full_linear(rows):
     results = _run(2, rows, "ok")
+    assert results == {0: True, 1: True}
+
+
+def test_chunked_block_cyclic_gather_matches_full_linear():
+    """4 chunks per rank, gathered asynchronously chunk by chunk."""
+    results = _run(2, 64, "ok", chunks=4)
     assert results == {0: True, 1: True}
 
 
