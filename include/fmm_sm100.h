@@ -52,8 +52,13 @@ typedef struct CUstream_st* fmm_stream_t; /* == cudaStream_t */
 /* bits of the device status word */
 #define FMM_STATUS_TIMEOUT 1u
 
+/* element types of A, weight/B, bias and C (the planes are always FP16) */
+#define FMM_DTYPE_BF16 0
+#define FMM_DTYPE_F16 1
+
 /* fmm_linear flags */
-#define FMM_LINEAR_PREPACKED 1u /* `weight_planes` already hold the packed Rt */
+#define FMM_LINEAR_PREPACKED 1u /* `Rt` already holds the packed right planes; W is ignored */
+#define FMM_RIGHT_KN 2u         /* W is a contiguous right matrix B[K,N] (plain mm), not weight[N,K] */
 
 typedef struct fmm_dims {
   int64_t scheme_size; /* s                      */
@@ -76,18 +81,26 @@ const char* fmm_last_error_string(void);
  * Replaces MatrixShape.from_dimensions (src/rdna3_fastmm/runtime.py:56-89). */
 int fmm_plan_dims(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* out);
 
-/* A[M,K] (BF16, lda) -> L[R][bm][ldk] (FP16).
+/* A[M,K] (BF16 or FP16 per dtype, lda) -> L[R][bm][ldk] (FP16).
  * Replaces left_transform_kernel (src/rdna3_fastmm/runtime.py:597-615;
  * src/rdna3_fastmm/generated/rank7_2x2x2.py:9-62 and the rank-48/49 twins). */
-int fmm_transform_a(int scheme, const void* A, int64_t M, int64_t K, int64_t lda, void* L,
-                    fmm_stream_t stream);
+int fmm_transform_a(int scheme, int dtype, const void* A, int64_t M, int64_t K, int64_t lda,
+                    void* L, fmm_stream_t stream);
 
-/* weight[N,K] (BF16, ldw) -> Rt[R][bn][ldk] (FP16), the transform of
+/* weight[N,K] (dtype, ldw) -> Rt[R][bn][ldk] (FP16), the transform of
  * B = weight^T stored K-major.  Used per call (dynamic) and once (prepack).
  * Replaces right_transform_weight_kernel (src/rdna3_fastmm/runtime.py:637-655;
  * src/rdna3_fastmm/generated/rank7_2x2x2.py:121-204 and twins). */
-int fmm_transform_w(int scheme, const void* W, int64_t N, int64_t K, int64_t ldw, void* Rt,
-                    fmm_stream_t stream);
+int fmm_transform_w(int scheme, int dtype, const void* W, int64_t N, int64_t K, int64_t ldw,
+                    void* Rt, fmm_stream_t stream);
+
+/* Contiguous right matrix B[K,N] (dtype, ldb) -> Rt[R][bn][ldk] (FP16), the
+ * same planes as fmm_transform_w of weight = B^T (transposed on chip).  The
+ * plain-mm API, per call and for pack_right.
+ * Replaces right_transform_kernel (src/rdna3_fastmm/runtime.py:617-635;
+ * src/rdna3_fastmm/generated/rank7_2x2x2.py:65-118 and twins). */
+int fmm_transform_b(int scheme, int dtype, const void* B, int64_t K, int64_t N, int64_t ldb,
+                    void* Rt, fmm_stream_t stream);
 
 /* P[r] = L[r] * Rt[r]^T for r < rank: FP16 operands, FP32 accumulation in
  * tensor memory, FP16 products.  tcgen05 + TMA, persistent over 148 SMs.
@@ -95,27 +108,28 @@ int fmm_transform_w(int scheme, const void* W, int64_t N, int64_t K, int64_t ldw
 int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
                   void* P, fmm_stream_t stream);
 
-/* P[R][bm][ldp] (FP16) -> C[M,N] (BF16, ldc) with optional bias[N] (BF16,
+/* P[R][bm][ldp] (FP16) -> C[M,N] (dtype, ldc) with optional bias[N] (dtype,
  * may be NULL): FP32 recombination, bias added last, round to nearest even.
  * Replaces output_transform_kernel / output_transform_bias_kernel
  * (src/rdna3_fastmm/runtime.py:657-698). */
-int fmm_reconstruct(int scheme, const void* P, int64_t M, int64_t N, const void* bias, void* C,
-                    int64_t ldc, fmm_stream_t stream);
+int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, const void* bias,
+                    void* C, int64_t ldc, fmm_stream_t stream);
 
-/* The whole F.linear: C = A * weight^T (+ bias) through the scheme, using the
- * caller's planes (L, Rt, P sized by fmm_plan_dims).  With
- * FMM_LINEAR_PREPACKED, `weight` is ignored (may be NULL) and `Rt` holds
- * planes produced earlier by fmm_transform_w.
- * Replaces _LinearPlan.run_linear / run_linear_packed
- * (src/rdna3_fastmm/runtime.py:700-777). */
-int fmm_linear(int scheme, const void* A, const void* W, const void* bias, void* C, int64_t M,
-               int64_t K, int64_t N, void* L, void* Rt, void* P, unsigned int flags,
+/* The whole product through the scheme, using the caller's planes (L, Rt, P
+ * sized by fmm_plan_dims): C = A * weight^T (+ bias) for F.linear, or, with
+ * FMM_RIGHT_KN, C = A * B for a contiguous B[K,N].  With FMM_LINEAR_PREPACKED,
+ * W is ignored (may be NULL) and Rt holds planes made earlier by
+ * fmm_transform_w / fmm_transform_b.
+ * Replaces _LinearPlan.run_linear / run_linear_packed and _Plan.run /
+ * run_packed (src/rdna3_fastmm/runtime.py:278-341, 700-777). */
+int fmm_linear(int scheme, int dtype, const void* A, const void* W, const void* bias, void* C,
+               int64_t M, int64_t K, int64_t N, void* L, void* Rt, void* P, unsigned int flags,
                fmm_stream_t stream);
 
 /* Size of the fixed scratch array behind fmm_linear_noalloc (32 MiB). */
 #define FMM_NOALLOC_SCRATCH_BYTES (32u << 20)
 
-/* fmm_linear without caller planes and without any allocation: for callers
+/* BF16 fmm_linear without caller planes and without any allocation: for callers
  * that are handed device buffers for A, weight, bias and C but cannot
  * allocate device memory themselves -- a plugin whose host application owns
  * and budgets all device memory, or a loop that must never call cudaMalloc

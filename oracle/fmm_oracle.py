@@ -192,8 +192,9 @@ def leaf_products(L: np.ndarray, R: np.ndarray) -> np.ndarray:
 
 
 def output_transform(name: str, P: np.ndarray, M: int, N: int,
-                     bias: np.ndarray | None = None) -> np.ndarray:
-    """P [R, bm, bn] float16 -> C [M, N] as float32 holding bf16 values."""
+                     bias: np.ndarray | None = None, out_dtype: str = "bf16") -> np.ndarray:
+    """P [R, bm, bn] float16 -> C [M, N] as float32 holding bf16 values
+    (``out_dtype="fp16"``: FP16 values, the reference's FP16-plan output)."""
     s, rank, _, _, output = scheme_circuits(name)
     bm, bn = P.shape[1], P.shape[2]
     outs = output.evaluate([P[r].astype(np.float32) for r in range(rank)])
@@ -205,6 +206,8 @@ def output_transform(name: str, P: np.ndarray, M: int, N: int,
             b[: bias.shape[0]] = bias.astype(np.float32)
             value = value + b[bc * bn:(bc + 1) * bn][None, :]
         C[br * bm:(br + 1) * bm, bc * bn:(bc + 1) * bn] = value
+    if out_dtype == "fp16":
+        return C[:M, :N].astype(np.float16).astype(np.float32)
     return bf16_round(C[:M, :N])
 
 

@@ -164,7 +164,7 @@ int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int 
   return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 
-template <int SCHEME, bool kWeight>
+template <int SCHEME, bool kWeight, bool kHalf>
 int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t ld, void* dst,
                            int64_t brows, int64_t bcols, int64_t ldd, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
@@ -173,16 +173,16 @@ int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t 
   const bool vec = (bcols % T::VEC == 0) && (ld % T::VEC == 0) && aligned(src, 2 * T::VEC);
   const int64_t items = brows * (ldd / T::VEC);
   using Prog = typename std::conditional<kWeight, typename T::Right, typename T::Left>::type;
-  block_transform_kernel<Prog, T::S, T::VEC, kWeight, T::kInThreads, T::kInBlocks>
+  block_transform_kernel<Prog, T::S, T::VEC, kWeight, T::kInThreads, T::kInBlocks, kHalf>
       <<<streaming_grid(info, items, T::kInThreads, T::kInGrid), T::kInThreads, 0, stream>>>(
-          static_cast<const __nv_bfloat16*>(src), rows, cols, ld, static_cast<__half*>(dst), brows,
+          static_cast<const uint16_t*>(src), rows, cols, ld, static_cast<__half*>(dst), brows,
           bcols, ldd, vec ? 1 : 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, kWeight ? "weight transform launch" : "left transform launch");
   return FMM_OK;
 }
 
-template <int SCHEME>
+template <int SCHEME, bool kHalf>
 int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                        void* C, int64_t ldc, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
@@ -191,13 +191,74 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
   if (int rc = device_info(&info)) return rc;
   const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
   const int64_t items = d.bm * ceil_div(d.bn, V);
-  reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks>
+  reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
       <<<streaming_grid(info, items, T::kOutThreads, T::kOutGrid), T::kOutThreads, 0, stream>>>(
-          static_cast<const __half*>(P), d.bm, d.bn, d.ldp,
-          static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(C), M, N, ldc,
-          vec ? 1 : 0);
+          static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
+          static_cast<uint16_t*>(C), M, N, ldc, vec ? 1 : 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
+  return FMM_OK;
+}
+
+template <int SCHEME, bool kHalf>
+int launch_right_kn(const void* B, int64_t K, int64_t N, int64_t ldb, void* dst, const fmm_dims& d,
+                    cudaStream_t stream) {
+  using T = SchemeTraits<SCHEME>;
+  constexpr int kTile = 32;
+  const dim3 grid(static_cast<unsigned>(ceil_div(d.ldk, kTile)),
+                  static_cast<unsigned>(ceil_div(d.bn, kTile)));
+  right_transform_kn_kernel<typename T::Right, T::S, kHalf, kTile><<<grid, 256, 0, stream>>>(
+      static_cast<const uint16_t*>(B), K, N, ldb, static_cast<__half*>(dst), d.bk, d.bn, d.ldk);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "right transform (K x N) launch");
+  return FMM_OK;
+}
+
+// Runtime (scheme, dtype) -> template instance.
+template <template <int, bool> class F, class... Args>
+int dispatch(int scheme, int dtype, Args... args) {
+  const bool half = dtype == FMM_DTYPE_F16;
+  switch (scheme) {
+    case FMM_SCHEME_RANK7:
+      return half ? F<FMM_SCHEME_RANK7, true>::run(args...) : F<FMM_SCHEME_RANK7, false>::run(args...);
+    case FMM_SCHEME_RANK48:
+      return half ? F<FMM_SCHEME_RANK48, true>::run(args...) : F<FMM_SCHEME_RANK48, false>::run(args...);
+    default:
+      return half ? F<FMM_SCHEME_RANK49, true>::run(args...) : F<FMM_SCHEME_RANK49, false>::run(args...);
+  }
+}
+template <int SC, bool H>
+struct LeftOp {
+  static int run(const void* A, int64_t M, int64_t K, int64_t lda, void* L, const fmm_dims* d,
+                 cudaStream_t s) {
+    return launch_input_transform<SC, false, H>(A, M, K, lda, L, d->bm, d->bk, d->ldk, s);
+  }
+};
+template <int SC, bool H>
+struct WeightOp {
+  static int run(const void* W, int64_t N, int64_t K, int64_t ldw, void* Rt, const fmm_dims* d,
+                 cudaStream_t s) {
+    return launch_input_transform<SC, true, H>(W, N, K, ldw, Rt, d->bn, d->bk, d->ldk, s);
+  }
+};
+template <int SC, bool H>
+struct RightKnOp {
+  static int run(const void* B, int64_t K, int64_t N, int64_t ldb, void* Rt, const fmm_dims* d,
+                 cudaStream_t s) {
+    return launch_right_kn<SC, H>(B, K, N, ldb, Rt, *d, s);
+  }
+};
+template <int SC, bool H>
+struct ReconstructOp {
+  static int run(const void* P, const fmm_dims* d, int64_t M, int64_t N, const void* bias, void* C,
+                 int64_t ldc, cudaStream_t s) {
+    return launch_reconstruct<SC, H>(P, *d, M, N, bias, C, ldc, s);
+  }
+};
+
+int check_dtype(int dtype) {
+  if (dtype != FMM_DTYPE_BF16 && dtype != FMM_DTYPE_F16)
+    return fail(FMM_ERR_UNSUPPORTED, "dtype must be FMM_DTYPE_BF16 or FMM_DTYPE_F16");
   return FMM_OK;
 }
 
@@ -420,40 +481,37 @@ int fmm_plan_dims(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* out) {
   return dims_for(scheme, M, K, N, out);
 }
 
-int fmm_transform_a(int scheme, const void* A, int64_t M, int64_t K, int64_t lda, void* L,
-                    fmm_stream_t stream) {
+int fmm_transform_a(int scheme, int dtype, const void* A, int64_t M, int64_t K, int64_t lda,
+                    void* L, fmm_stream_t stream) {
   fmm_dims d;
   if (int rc = dims_for(scheme, M, K, 1, &d)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
   if (A == nullptr || L == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
   if (lda < K) return fail(FMM_ERR_INVALID_ARGUMENT, "lda < K");
   if (!aligned(L, 16)) return fail(FMM_ERR_MISALIGNED, "L must be 16-byte aligned");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (scheme) {
-    case FMM_SCHEME_RANK7:
-      return launch_input_transform<FMM_SCHEME_RANK7, false>(A, M, K, lda, L, d.bm, d.bk, d.ldk, s);
-    case FMM_SCHEME_RANK48:
-      return launch_input_transform<FMM_SCHEME_RANK48, false>(A, M, K, lda, L, d.bm, d.bk, d.ldk, s);
-    default:
-      return launch_input_transform<FMM_SCHEME_RANK49, false>(A, M, K, lda, L, d.bm, d.bk, d.ldk, s);
-  }
+  return dispatch<LeftOp>(scheme, dtype, A, M, K, lda, L, &d, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int fmm_transform_w(int scheme, const void* W, int64_t N, int64_t K, int64_t ldw, void* Rt,
-                    fmm_stream_t stream) {
+int fmm_transform_w(int scheme, int dtype, const void* W, int64_t N, int64_t K, int64_t ldw,
+                    void* Rt, fmm_stream_t stream) {
   fmm_dims d;
   if (int rc = dims_for(scheme, 1, K, N, &d)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
   if (W == nullptr || Rt == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
   if (ldw < K) return fail(FMM_ERR_INVALID_ARGUMENT, "ldw < K");
   if (!aligned(Rt, 16)) return fail(FMM_ERR_MISALIGNED, "Rt must be 16-byte aligned");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (scheme) {
-    case FMM_SCHEME_RANK7:
-      return launch_input_transform<FMM_SCHEME_RANK7, true>(W, N, K, ldw, Rt, d.bn, d.bk, d.ldk, s);
-    case FMM_SCHEME_RANK48:
-      return launch_input_transform<FMM_SCHEME_RANK48, true>(W, N, K, ldw, Rt, d.bn, d.bk, d.ldk, s);
-    default:
-      return launch_input_transform<FMM_SCHEME_RANK49, true>(W, N, K, ldw, Rt, d.bn, d.bk, d.ldk, s);
-  }
+  return dispatch<WeightOp>(scheme, dtype, W, N, K, ldw, Rt, &d, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fmm_transform_b(int scheme, int dtype, const void* B, int64_t K, int64_t N, int64_t ldb,
+                    void* Rt, fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, 1, K, N, &d)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (B == nullptr || Rt == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ldb < N) return fail(FMM_ERR_INVALID_ARGUMENT, "ldb < N");
+  if (!aligned(Rt, 16)) return fail(FMM_ERR_MISALIGNED, "Rt must be 16-byte aligned");
+  return dispatch<RightKnOp>(scheme, dtype, B, K, N, ldb, Rt, &d, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
@@ -463,36 +521,36 @@ int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t b
   return launch_leaf_gemm(rank, L, Rt, bm, bn, bk, P, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int fmm_reconstruct(int scheme, const void* P, int64_t M, int64_t N, const void* bias, void* C,
-                    int64_t ldc, fmm_stream_t stream) {
+int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, const void* bias,
+                    void* C, int64_t ldc, fmm_stream_t stream) {
   fmm_dims d;
   if (int rc = dims_for(scheme, M, 1, N, &d)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
   if (P == nullptr || C == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
   if (ldc < N) return fail(FMM_ERR_INVALID_ARGUMENT, "ldc < N");
   if (!aligned(P, 16)) return fail(FMM_ERR_MISALIGNED, "P must be 16-byte aligned");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (scheme) {
-    case FMM_SCHEME_RANK7: return launch_reconstruct<FMM_SCHEME_RANK7>(P, d, M, N, bias, C, ldc, s);
-    case FMM_SCHEME_RANK48: return launch_reconstruct<FMM_SCHEME_RANK48>(P, d, M, N, bias, C, ldc, s);
-    default: return launch_reconstruct<FMM_SCHEME_RANK49>(P, d, M, N, bias, C, ldc, s);
-  }
+  return dispatch<ReconstructOp>(scheme, dtype, P, &d, M, N, bias, C, ldc,
+                                 reinterpret_cast<cudaStream_t>(stream));
 }
 
-int fmm_linear(int scheme, const void* A, const void* W, const void* bias, void* C, int64_t M,
-               int64_t K, int64_t N, void* L, void* Rt, void* P, unsigned int flags,
+int fmm_linear(int scheme, int dtype, const void* A, const void* W, const void* bias, void* C,
+               int64_t M, int64_t K, int64_t N, void* L, void* Rt, void* P, unsigned int flags,
                fmm_stream_t stream) {
   fmm_dims d;
   if (int rc = dims_for(scheme, M, K, N, &d)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
   if (A == nullptr || C == nullptr || L == nullptr || Rt == nullptr || P == nullptr)
     return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
   const bool prepacked = (flags & FMM_LINEAR_PREPACKED) != 0;
   if (!prepacked && W == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null weight");
-  if (int rc = fmm_transform_a(scheme, A, M, K, K, L, stream)) return rc;
+  if (int rc = fmm_transform_a(scheme, dtype, A, M, K, K, L, stream)) return rc;
   if (!prepacked) {
-    if (int rc = fmm_transform_w(scheme, W, N, K, K, Rt, stream)) return rc;
+    const int rc = (flags & FMM_RIGHT_KN) ? fmm_transform_b(scheme, dtype, W, K, N, N, Rt, stream)
+                                          : fmm_transform_w(scheme, dtype, W, N, K, K, Rt, stream);
+    if (rc) return rc;
   }
   if (int rc = fmm_leaf_gemm(static_cast<int>(d.rank), L, Rt, d.bm, d.bn, d.bk, P, stream)) return rc;
-  return fmm_reconstruct(scheme, P, M, N, bias, C, N, stream);
+  return fmm_reconstruct(scheme, dtype, P, M, N, bias, C, N, stream);
 }
 
 int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bias, void* C,
@@ -516,8 +574,8 @@ int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bia
   unsigned char* bytes = static_cast<unsigned char*>(base);
   // Every plane element the GEMM and the reconstruct read is written earlier
   // in the same call (pitch padding included), so nothing is cleared first.
-  return fmm_linear(scheme, A, W, bias, C, M, K, N, bytes, bytes + left, bytes + left + right, 0u,
-                    stream);
+  return fmm_linear(scheme, FMM_DTYPE_BF16, A, W, bias, C, M, K, N, bytes, bytes + left,
+                    bytes + left + right, 0u, stream);
 }
 
 int fmm_set_sm_budget(int sms) {

@@ -95,6 +95,16 @@ __device__ __forceinline__ VecF<N> unpack_half(const typename VecIO<N>::H& raw) 
   return r;
 }
 
+// 16-bit element types of the operands: BF16 (kHalf = false) or FP16.
+template <bool kHalf, int N>
+__device__ __forceinline__ VecF<N> unpack_in(const typename VecIO<N>::BF& raw) {
+  if constexpr (kHalf) {
+    return unpack_half<N>(raw);
+  } else {
+    return unpack_bf16<N>(raw);
+  }
+}
+
 template <int N>
 __device__ __forceinline__ void store_half_vec(__half* p, const VecF<N>& x) {
   typename VecIO<N>::H raw;
@@ -111,6 +121,32 @@ __device__ __forceinline__ void store_bf16_vec(__nv_bfloat16* p, const VecF<N>& 
 #pragma unroll
   for (int i = 0; i < N / 2; ++i) h[i] = __floats2bfloat162_rn(x.v[2 * i], x.v[2 * i + 1]);
   *reinterpret_cast<typename VecIO<N>::BF*>(p) = raw;
+}
+
+// Output element (BF16 or FP16), round to nearest even.
+template <bool kHalf>
+__device__ __forceinline__ uint16_t round_out(float x) {
+  if constexpr (kHalf) {
+    return __half_as_ushort(__float2half_rn(x));
+  } else {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  }
+}
+template <bool kHalf>
+__device__ __forceinline__ float widen_in(uint16_t bits) {
+  if constexpr (kHalf) {
+    return __half2float(__ushort_as_half(bits));
+  } else {
+    return __bfloat162float(__ushort_as_bfloat16(bits));
+  }
+}
+template <bool kHalf, int N>
+__device__ __forceinline__ void store_out_vec(uint16_t* p, const VecF<N>& x) {
+  if constexpr (kHalf) {
+    store_half_vec<N>(reinterpret_cast<__half*>(p), x);
+  } else {
+    store_bf16_vec<N>(reinterpret_cast<__nv_bfloat16*>(p), x);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -133,9 +169,10 @@ __device__ __forceinline__ void store_bf16_vec(__nv_bfloat16* p, const VecF<N>& 
 // as it needs them.  This memory-level parallelism is what keeps the rank-48/49
 // transforms near HBM bandwidth.  Columns in [bcols, ldd) are padding and are
 // written as zeros.
-template <class Prog, int S, int VEC, bool kWeight, int THREADS = 256, int MIN_BLOCKS = 1>
+template <class Prog, int S, int VEC, bool kWeight, int THREADS = 256, int MIN_BLOCKS = 1,
+          bool kHalfIn = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
-    const __nv_bfloat16* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
+    const uint16_t* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
     __half* __restrict__ dst, int64_t brows, int64_t bcols, int64_t ldd, int vector_loads) {
   using Raw = typename VecIO<VEC>::BF;
   const int64_t plane = brows * ldd;
@@ -165,15 +202,15 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
         const int bc = kWeight ? (q / S) : (q % S);
         const int64_t r = br * brows + i;
         const int64_t c0 = bc * bcols + j;
-        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw[q]);
+        uint16_t* e = reinterpret_cast<uint16_t*>(&raw[q]);
 #pragma unroll
         for (int k = 0; k < VEC; ++k) {
           const bool ok = r < rows && j + k < bcols && c0 + k < cols;
-          e[k] = ok ? src[r * ld + c0 + k] : __float2bfloat16(0.0f);
+          e[k] = ok ? src[r * ld + c0 + k] : uint16_t(0);  // +0 in both formats
         }
       }
     }
-    auto in = [&](int q) -> VecF<VEC> { return unpack_bf16<VEC>(raw[q]); };
+    auto in = [&](int q) -> VecF<VEC> { return unpack_in<kHalfIn, VEC>(raw[q]); };
     auto out = [&](int o, const VecF<VEC>& x) {
       store_half_vec<VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
     };
@@ -186,10 +223,10 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
 // Output o is C block (o / S, o % S); bias[bc*bn + c] is added after the whole
 // recombination, then rounded to nearest even BF16.  As in the input side, all
 // R product vectors are loaded before the arithmetic.
-template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1>
+template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
     const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
-    const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ C, int64_t M, int64_t N,
+    const uint16_t* __restrict__ bias, uint16_t* __restrict__ C, int64_t M, int64_t N,
     int64_t ldc, int vector_stores) {
   using Raw = typename VecIO<VEC>::H;
   const int64_t plane = bm * ldp;
@@ -214,17 +251,63 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
         VecF<VEC> b;
 #pragma unroll
         for (int e = 0; e < VEC; ++e)
-          b.v[e] = (j + e < bn && c0 + e < N) ? __bfloat162float(bias[c0 + e]) : 0.0f;
+          b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
         y = vadd(x, b);
       }
-      __nv_bfloat16* dst = C + row * ldc + c0;
+      uint16_t* dst = C + row * ldc + c0;
       if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
-        store_bf16_vec<VEC>(dst, y);
+        store_out_vec<kHalfOut, VEC>(dst, y);
       } else {
 #pragma unroll
         for (int e = 0; e < VEC; ++e)
-          if (j + e < bn && c0 + e < N) dst[e] = __float2bfloat16_rn(y.v[e]);
+          if (j + e < bn && c0 + e < N) dst[e] = round_out<kHalfOut>(y.v[e]);
       }
+    };
+    Prog::template run<VecF<VEC>>(in, out);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Right transform of a contiguous B[K, N] (the plain-mm API): the program's
+// input q is block (q / S, q % S) of B and the planes come out K-major,
+// Rt[r][n][k], so each block is transposed on the way.  A CTA owns one
+// TILE x TILE position (k0, n0) inside the blocks: it stages the S*S input
+// tiles in shared memory with row loads along n (coalesced), then each thread
+// evaluates the program for VEC consecutive k at one n, reading the staged
+// tiles down a column, and stores VEC elements along k (coalesced).
+template <class Prog, int S, bool kHalfIn, int TILE = 32, int VEC = 4>
+__global__ void __launch_bounds__(256) right_transform_kn_kernel(
+    const uint16_t* __restrict__ B, int64_t K, int64_t N, int64_t ldb, __half* __restrict__ dst,
+    int64_t bk, int64_t bn, int64_t ldk) {
+  constexpr int Q = S * S;
+  __shared__ uint16_t tile[Q][TILE][TILE + 2];
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * TILE;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * TILE;
+  for (int idx = threadIdx.x; idx < Q * TILE * TILE; idx += blockDim.x) {
+    const int q = idx / (TILE * TILE);
+    const int kk = (idx / TILE) % TILE;
+    const int nn = idx % TILE;
+    const int64_t k = k0 + kk, n = n0 + nn;
+    const int64_t row = (q / S) * bk + k, col = (q % S) * bn + n;
+    const bool ok = k < bk && n < bn && row < K && col < N;
+    tile[q][kk][nn] = ok ? B[row * ldb + col] : uint16_t(0);
+  }
+  __syncthreads();
+  const int64_t plane = bn * ldk;
+  constexpr int kVecsPerColumn = TILE / VEC;
+  for (int idx = threadIdx.x; idx < TILE * kVecsPerColumn; idx += blockDim.x) {
+    const int nn = idx / kVecsPerColumn;
+    const int kk = (idx % kVecsPerColumn) * VEC;
+    const int64_t n = n0 + nn, k = k0 + kk;
+    if (n >= bn || k >= ldk) continue;
+    auto in = [&](int q) -> VecF<VEC> {
+      VecF<VEC> x;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) x.v[e] = widen_in<kHalfIn>(tile[q][kk + e][nn]);
+      return x;
+    };
+    auto out = [&](int o, const VecF<VEC>& x) {
+      store_half_vec<VEC>(dst + o * plane + n * ldk + k, x);
     };
     Prog::template run<VecF<VEC>>(in, out);
   }

@@ -22,6 +22,9 @@ FMM_ERR_DEVICE_TIMEOUT = 5
 FMM_ERR_TOO_LARGE = 6
 FMM_STATUS_TIMEOUT = 1
 FMM_LINEAR_PREPACKED = 1
+FMM_RIGHT_KN = 2
+FMM_DTYPE_BF16 = 0
+FMM_DTYPE_F16 = 1
 
 SCHEME_IDS = {"rank7": 7, "rank48": 48, "rank49": 49}
 
@@ -51,12 +54,13 @@ _SIGNATURES = {
     "fmm_version": ([], ctypes.c_int),
     "fmm_last_error_string": ([], ctypes.c_char_p),
     "fmm_plan_dims": ([ctypes.c_int, _I64, _I64, _I64, ctypes.POINTER(FmmDims)], ctypes.c_int),
-    "fmm_transform_a": ([ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
-    "fmm_transform_w": ([ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_transform_a": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_transform_w": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_transform_b": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_leaf_gemm": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
-    "fmm_reconstruct": ([ctypes.c_int, _P, _I64, _I64, _P, _P, _I64, _P], ctypes.c_int),
+    "fmm_reconstruct": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _P, _P, _I64, _P], ctypes.c_int),
     "fmm_linear": (
-        [ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, ctypes.c_uint, _P],
+        [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, ctypes.c_uint, _P],
         ctypes.c_int,
     ),
     "fmm_linear_noalloc": ([ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P], ctypes.c_int),
@@ -118,16 +122,32 @@ def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def dtype_id(dtype) -> int:
+    import torch
+
+    if dtype == torch.bfloat16:
+        return FMM_DTYPE_BF16
+    if dtype == torch.float16:
+        return FMM_DTYPE_F16
+    raise ValueError(f"libfmm_sm100 takes BF16 or FP16 operands, not {dtype}")
+
+
 def transform_a(scheme: str, A, L) -> None:
     M, K = A.shape
-    check(library().fmm_transform_a(SCHEME_IDS[scheme], _ptr(A), M, K, A.stride(0), _ptr(L),
-                                    _stream(A.device)), "fmm_transform_a")
+    check(library().fmm_transform_a(SCHEME_IDS[scheme], dtype_id(A.dtype), _ptr(A), M, K, A.stride(0),
+                                    _ptr(L), _stream(A.device)), "fmm_transform_a")
 
 
 def transform_w(scheme: str, W, Rt) -> None:
     N, K = W.shape
-    check(library().fmm_transform_w(SCHEME_IDS[scheme], _ptr(W), N, K, W.stride(0), _ptr(Rt),
-                                    _stream(W.device)), "fmm_transform_w")
+    check(library().fmm_transform_w(SCHEME_IDS[scheme], dtype_id(W.dtype), _ptr(W), N, K, W.stride(0),
+                                    _ptr(Rt), _stream(W.device)), "fmm_transform_w")
+
+
+def transform_b(scheme: str, B, Rt) -> None:
+    K, N = B.shape
+    check(library().fmm_transform_b(SCHEME_IDS[scheme], dtype_id(B.dtype), _ptr(B), K, N, B.stride(0),
+                                    _ptr(Rt), _stream(B.device)), "fmm_transform_b")
 
 
 def leaf_gemm(rank: int, L, Rt, bm: int, bn: int, bk: int, P) -> None:
@@ -136,16 +156,19 @@ def leaf_gemm(rank: int, L, Rt, bm: int, bn: int, bk: int, P) -> None:
 
 
 def reconstruct(scheme: str, P, M: int, N: int, bias, C) -> None:
-    check(library().fmm_reconstruct(SCHEME_IDS[scheme], _ptr(P), M, N, _ptr(bias), _ptr(C),
-                                    C.stride(0), _stream(P.device)), "fmm_reconstruct")
+    check(library().fmm_reconstruct(SCHEME_IDS[scheme], dtype_id(C.dtype), _ptr(P), M, N, _ptr(bias),
+                                    _ptr(C), C.stride(0), _stream(P.device)), "fmm_reconstruct")
 
 
-def linear(scheme: str, A, W, bias, C, L, Rt, P, prepacked: bool) -> None:
+def linear(scheme: str, A, W, bias, C, L, Rt, P, prepacked: bool, right_kn: bool = False) -> None:
+    """C = A @ W^T (+ bias); with ``right_kn`` W is a [K, N] right matrix and
+    C = A @ W.  ``prepacked``: Rt already holds the right planes."""
     M, K = A.shape
     N = C.shape[1]
-    flags = FMM_LINEAR_PREPACKED if prepacked else 0
-    check(library().fmm_linear(SCHEME_IDS[scheme], _ptr(A), _ptr(W), _ptr(bias), _ptr(C), M, K, N,
-                               _ptr(L), _ptr(Rt), _ptr(P), flags, _stream(A.device)), "fmm_linear")
+    flags = (FMM_LINEAR_PREPACKED if prepacked else 0) | (FMM_RIGHT_KN if right_kn else 0)
+    check(library().fmm_linear(SCHEME_IDS[scheme], dtype_id(A.dtype), _ptr(A), _ptr(W), _ptr(bias),
+                               _ptr(C), M, K, N, _ptr(L), _ptr(Rt), _ptr(P), flags, _stream(A.device)),
+          "fmm_linear")
 
 
 def linear_noalloc(scheme: str, A, W, bias, C) -> int:

@@ -1,11 +1,12 @@
 """Inductor ``external_matmul`` callable (reference ``external_mm.py:1-48``).
 
 ``rdna3_rank49_dynamic_v1_out(left, right, *, out)`` is offered to Inductor's
-GEMM autotuner.  It runs a reduced-rank plan only for FP16 ``left @ right``
-shapes in ``Rank49Plan.dynamic_shapes`` (the plain-mm API's measured table);
-every other call is ``torch.mm(left, right, out=out)``, exactly as in the
-reference.  The B200 table of the plain-mm API is empty (that API is not
-built yet), so the callable is the library product for every shape today.
+GEMM autotuner.  It runs ``Rank49Plan.run`` only for FP16 ``left @ right``
+shapes in ``Rank49Plan.dynamic_shapes`` (the plain-mm API's measured table)
+and when the workspace fits in free memory; every other call is
+``torch.mm(left, right, out=out)``, exactly as in the reference.  No plain-mm
+shape beats cuBLAS on B200, so that table is empty and the callable is the
+library product for every shape.
 """
 
 from __future__ import annotations
@@ -41,4 +42,11 @@ def rdna3_rank49_dynamic_v1_out(left: torch.Tensor, right: torch.Tensor, *, out:
     if not is_rank49_dynamic_eligible(left, right, out):
         torch.mm(left, right, out=out)
         return
-    raise NotImplementedError("the plain-mm reduced-rank API is not built for B200 yet")
+    rows, inner = left.shape
+    columns = right.shape[1]
+    plan = Rank49Plan(rows, inner, columns, left.device, left.dtype)
+    free_bytes, _ = torch.cuda.mem_get_info(left.device)
+    if plan.workspace_bytes > free_bytes:
+        torch.mm(left, right, out=out)
+        return
+    plan.run(left, right, plan.allocate_workspace(max_free_memory_fraction=1.0), out)

@@ -61,10 +61,10 @@ def _run_linear(plan_type: type[_LinearPlan], input_tensor: torch.Tensor, weight
 
 def _check_operands(input_tensor: torch.Tensor, weight: torch.Tensor,
                     bias: Optional[torch.Tensor]) -> None:
-    if input_tensor.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
-        raise ValueError("rdna3_fastmm linear operators take BF16 input and weight")
-    if bias is not None and bias.dtype != torch.bfloat16:
-        raise ValueError("rdna3_fastmm linear operators take a BF16 bias")
+    if input_tensor.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != input_tensor.dtype:
+        raise ValueError("rdna3_fastmm linear operators take BF16 or FP16 input and weight of one dtype")
+    if bias is not None and bias.dtype != input_tensor.dtype:
+        raise ValueError("rdna3_fastmm linear operators take a bias of the input's dtype")
     if weight.ndim != 2 or input_tensor.shape[-1] != weight.shape[1]:
         raise ValueError("input and weight shapes do not form a linear")
     if bias is not None and tuple(bias.shape) != (weight.shape[0],):

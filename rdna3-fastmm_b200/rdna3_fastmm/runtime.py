@@ -168,6 +168,9 @@ class _LinearPlan:
     rank: int
     scheme_size: int
     precision_pairs: frozenset
+    # plain-mm API tables (FP16 in, FP16 out): shapes measured to win on B200
+    dynamic_shapes: frozenset = frozenset()
+    prepacked_shapes: frozenset = frozenset()
     linear_shape_families: tuple[LinearShapeFamily, ...] = ()
     prepacked_linear_shape_families: tuple[LinearShapeFamily, ...] = ()
     transform_vector: int = 4
@@ -221,6 +224,16 @@ class _LinearPlan:
         return elements * self.compute_dtype.itemsize
 
     # ------------------------------------------------------------------ gate
+    def is_recommended(self, *, prepacked_right: bool = False) -> bool:
+        """Plain-mm gate (reference ``runtime.py:207-214``)."""
+        shapes = self.prepacked_shapes if prepacked_right else self.dynamic_shapes
+        return (
+            self.dtype == torch.float16
+            and self.compute_dtype == torch.float16
+            and self.shape.dimensions in shapes
+            and is_tested_runtime(self.device)
+        )
+
     @classmethod
     def has_measured_linear_win(cls, shape: tuple[int, int, int], *, has_bias: bool,
                                 prepacked_weight: bool = False) -> bool:
@@ -291,7 +304,52 @@ class _LinearPlan:
         return PackedWeight(self.algorithm, self.dtype, self.compute_dtype, transformed,
                             (s.columns, s.inner))
 
+    def pack_right(self, right: torch.Tensor, max_free_memory_fraction: float = 0.75) -> PackedRight:
+        """Transform a contiguous right matrix ``[K, N]`` once on the device."""
+        self._validate_right(right)
+        self._ensure_memory_budget(self.packed_right_bytes, max_free_memory_fraction,
+                                   f"{self.algorithm} packed right matrix")
+        transformed = self._planes("right")
+        with torch.cuda.device(self.device):
+            _native.transform_b(self.scheme, right, transformed)
+        s = self.shape
+        return PackedRight(self.algorithm, self.dtype, self.compute_dtype, transformed, (s.inner, s.columns))
+
     # ------------------------------------------------------------------ run
+    def run(self, left: torch.Tensor, right: torch.Tensor, workspace: Workspace,
+            output: torch.Tensor | None = None) -> torch.Tensor:
+        """``left @ right`` for contiguous ``left[M, K]`` and ``right[K, N]``
+        (reference ``runtime.py:278-308``)."""
+        self._validate_left(left)
+        self._validate_right(right)
+        self._validate_workspace(workspace, require_right=True)
+        result = self._output(output)
+        self._validate_output_storage(result, left, right, workspace.left_transformed,
+                                      workspace.products, workspace.right_transformed)
+        right_planes = workspace.right_transformed
+        if right_planes is None:
+            raise ValueError("dynamic execution requires a dynamic workspace")
+        with torch.cuda.device(self.device):
+            _native.linear(self.scheme, left, right, None, result, workspace.left_transformed,
+                           right_planes, workspace.products, prepacked=False, right_kn=True)
+        return result
+
+    def run_packed(self, left: torch.Tensor, right: PackedRight, workspace: Workspace,
+                   output: torch.Tensor | None = None) -> torch.Tensor:
+        """``left @ right`` with the right matrix packed by ``pack_right``
+        (reference ``runtime.py:310-341``)."""
+        self._validate_left(left)
+        self._validate_packed_right(right)
+        self._validate_workspace(workspace, require_right=False)
+        result = self._output(output)
+        self._validate_separate_storage(right.transformed, workspace.left_transformed, workspace.products)
+        self._validate_output_storage(result, left, right.transformed, workspace.left_transformed,
+                                      workspace.products, workspace.right_transformed)
+        with torch.cuda.device(self.device):
+            _native.linear(self.scheme, left, None, None, result, workspace.left_transformed,
+                           right.transformed, workspace.products, prepacked=True)
+        return result
+
     def run_linear(self, input_tensor: torch.Tensor, weight: torch.Tensor, workspace: Workspace,
                    bias: torch.Tensor | None = None, output: torch.Tensor | None = None) -> torch.Tensor:
         self._validate_left(input_tensor)
@@ -333,6 +391,9 @@ class _LinearPlan:
     def _validate_left(self, tensor: torch.Tensor) -> None:
         self._validate_tensor(tensor, (self.shape.rows, self.shape.inner), "left")
 
+    def _validate_right(self, tensor: torch.Tensor) -> None:
+        self._validate_tensor(tensor, (self.shape.inner, self.shape.columns), "right")
+
     def _validate_weight(self, tensor: torch.Tensor) -> None:
         self._validate_tensor(tensor, (self.shape.columns, self.shape.inner), "weight")
 
@@ -372,16 +433,26 @@ class _LinearPlan:
     def _validate_packed_weight(self, packed: PackedWeight) -> None:
         if not isinstance(packed, PackedWeight):
             raise ValueError("packed Linear weight does not match the plan")
+        s = self.shape
+        self._validate_packed(packed, (s.columns, s.inner), "Linear weight")
+
+    def _validate_packed_right(self, packed: PackedRight) -> None:
+        if not isinstance(packed, PackedRight):
+            raise ValueError("packed right matrix does not match the plan")
+        s = self.shape
+        self._validate_packed(packed, (s.inner, s.columns), "right matrix")
+
+    def _validate_packed(self, packed: _PackedTransform, source_shape: tuple[int, int], name: str) -> None:
         if (packed.algorithm != self.algorithm or packed.source_dtype != self.dtype
                 or packed.compute_dtype != self.compute_dtype):
-            raise ValueError("packed Linear weight does not match the plan")
+            raise ValueError(f"packed {name} does not match the plan")
         s = self.shape
-        if packed.source_shape != (s.columns, s.inner):
-            raise ValueError("packed Linear weight shape does not match the plan")
+        if packed.source_shape != source_shape:
+            raise ValueError(f"packed {name} shape does not match the plan")
         t = packed.transformed
         if (tuple(t.shape) != (self.rank, s.block_columns, s.inner_pitch) or t.device != self.device
                 or t.dtype != self.compute_dtype or not t.is_contiguous() or t.requires_grad):
-            raise ValueError("packed Linear weight does not match the plan")
+            raise ValueError(f"packed {name} does not match the plan")
 
     def _output(self, output: torch.Tensor | None) -> torch.Tensor:
         shape = (self.shape.rows, self.shape.columns)
@@ -410,6 +481,10 @@ def _overlaps(first: torch.Tensor, second: torch.Tensor) -> bool:
 
 
 _BF16_FP16 = frozenset({(torch.bfloat16, torch.float16)})
+# FP16 inputs with FP16 leaves, as the reference's rank-7 and rank-49 plans
+# allow; BF16 leaf products (the reference's (bf16, bf16) rank-49 pair) are not
+# built for B200
+_FP16_AND_BF16_FP16 = frozenset({(torch.float16, torch.float16), (torch.bfloat16, torch.float16)})
 
 
 class Rank7Plan(_LinearPlan):
@@ -419,7 +494,7 @@ class Rank7Plan(_LinearPlan):
     scheme = "rank7"
     rank = 7
     scheme_size = 2
-    precision_pairs = _BF16_FP16
+    precision_pairs = _FP16_AND_BF16_FP16
     transform_vector = 8
     # B200 measurements against cuBLAS BF16 (F.linear): no shape has won yet,
     # so nothing is routed here by the graph rewrite.
@@ -446,7 +521,7 @@ class Rank49Plan(_LinearPlan):
     scheme = "rank49"
     rank = 49
     scheme_size = 4
-    precision_pairs = _BF16_FP16
+    precision_pairs = _FP16_AND_BF16_FP16
     linear_shape_families: tuple[LinearShapeFamily, ...] = ()
     prepacked_linear_shape_families: tuple[LinearShapeFamily, ...] = ()
 

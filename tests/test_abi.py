@@ -54,7 +54,9 @@ def test_host_side_errors_need_no_gpu():
     assert lib.fmm_plan_dims(5, 4, 4, 4, ctypes.byref(dims)) == _native.FMM_ERR_UNSUPPORTED
     assert "unknown scheme" in _native.last_error()
     assert lib.fmm_plan_dims(7, 0, 4, 4, ctypes.byref(dims)) == _native.FMM_ERR_INVALID_ARGUMENT
-    assert lib.fmm_transform_a(7, None, 4, 4, 4, None, None) == _native.FMM_ERR_INVALID_ARGUMENT
+    assert lib.fmm_transform_a(7, 0, None, 4, 4, 4, None, None) == _native.FMM_ERR_INVALID_ARGUMENT
+    fake_ptr = ctypes.c_void_p(0x1000)
+    assert lib.fmm_transform_a(7, 5, fake_ptr, 4, 4, 4, fake_ptr, None) == _native.FMM_ERR_UNSUPPORTED
     assert lib.fmm_set_wait_timeout_ns(0) == _native.FMM_ERR_INVALID_ARGUMENT
     fake = ctypes.c_void_p(0x1000)
     rc = lib.fmm_linear_noalloc(7, fake, fake, None, fake, 8192, 8192, 8192, None)

@@ -85,9 +85,25 @@ def test_plan_rejects_cpu_device(plan):
 def test_plan_rejects_unsupported_precision(monkeypatch, plan):
     configure_supported_runtime(monkeypatch)
     with pytest.raises(ValueError, match="does not support"):
-        plan(4, 4, 4, torch.device("cuda", 0), dtype=torch.float16)
-    with pytest.raises(ValueError, match="does not support"):
         plan(4, 4, 4, torch.device("cuda", 0), dtype=torch.bfloat16, compute_dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="does not support"):
+        plan(4, 4, 4, torch.device("cuda", 0), dtype=torch.float32)
+
+
+def test_precision_pairs_follow_the_reference(monkeypatch):
+    """FP16 plans exist for rank 7 and rank 49 (reference runtime.py:785-790,
+    852-858); rank 48 is BF16-in only (:828)."""
+    configure_supported_runtime(monkeypatch)
+    for plan in (Rank7Plan, Rank49Plan):
+        p = plan(4, 4, 4, torch.device("cuda", 0))  # default dtype FP16
+        assert (p.dtype, p.compute_dtype) == (torch.float16, torch.float16)
+    with pytest.raises(ValueError, match="does not support"):
+        Rank48Plan(4, 4, 4, torch.device("cuda", 0))
+
+
+def test_mm_tables_hold_only_measured_b200_wins():
+    for plan in (Rank7Plan, Rank48Plan, Rank49Plan):
+        assert plan.dynamic_shapes == frozenset() and plan.prepacked_shapes == frozenset()
 
 
 @pytest.mark.parametrize("plan,rank,s", [(Rank7Plan, 7, 2), (Rank48Plan, 48, 4), (Rank49Plan, 49, 4)])
