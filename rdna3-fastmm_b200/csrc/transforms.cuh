@@ -219,10 +219,46 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Output side (unfused reconstruct): P[r][bm][ldp] FP16 -> C[M,N] BF16.
-// Output o is C block (o / S, o % S); bias[bc*bn + c] is added after the whole
-// recombination, then rounded to nearest even BF16.  As in the input side, all
-// R product vectors are loaded before the arithmetic.
+// Output side: recombine one vector position (plane row i, columns j..j+VEC)
+// of the R product planes into the S*S output blocks of C.  Output o is C
+// block (o / S, o % S); bias[bc*bn + c] is added after the whole
+// recombination, then rounded to nearest even (BF16 or FP16).  `raw` holds the
+// R product vectors, already loaded.  Shared by the reconstruct kernel and the
+// fused rank-7 epilogue of the leaf GEMM, so both round identically.
+template <class Prog, int S, int VEC, bool kHalfOut>
+__device__ __forceinline__ void recombine_vector(const typename VecIO<VEC>::H (&raw)[Prog::kInputs],
+                                                 int64_t i, int64_t j, int64_t bm, int64_t bn,
+                                                 const uint16_t* __restrict__ bias,
+                                                 uint16_t* __restrict__ C, int64_t M, int64_t N,
+                                                 int64_t ldc, int vector_stores) {
+  auto in = [&](int r) -> VecF<VEC> { return unpack_half<VEC>(raw[r]); };
+  auto out = [&](int o, const VecF<VEC>& x) {
+    const int br = o / S, bc = o % S;
+    const int64_t row = br * bm + i;
+    if (row >= M) return;
+    const int64_t c0 = bc * bn + j;
+    VecF<VEC> y = x;
+    if (bias != nullptr) {
+      VecF<VEC> b;
+#pragma unroll
+      for (int e = 0; e < VEC; ++e)
+        b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
+      y = vadd(x, b);
+    }
+    uint16_t* dst = C + row * ldc + c0;
+    if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
+      store_out_vec<kHalfOut, VEC>(dst, y);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e)
+        if (j + e < bn && c0 + e < N) dst[e] = round_out<kHalfOut>(y.v[e]);
+    }
+  };
+  Prog::template run<VecF<VEC>>(in, out);
+}
+
+// Unfused reconstruct: P[r][bm][ldp] FP16 -> C[M,N].  All R product vectors
+// are loaded before the arithmetic, as in the input side.
 template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
     const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
@@ -240,30 +276,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
 #pragma unroll
     for (int r = 0; r < Prog::kInputs; ++r)
       raw[r] = __ldg(reinterpret_cast<const Raw*>(P + r * plane + static_cast<int64_t>(i) * ldp + j));
-    auto in = [&](int r) -> VecF<VEC> { return unpack_half<VEC>(raw[r]); };
-    auto out = [&](int o, const VecF<VEC>& x) {
-      const int br = o / S, bc = o % S;
-      const int64_t row = br * bm + i;
-      if (row >= M) return;
-      const int64_t c0 = bc * bn + j;
-      VecF<VEC> y = x;
-      if (bias != nullptr) {
-        VecF<VEC> b;
-#pragma unroll
-        for (int e = 0; e < VEC; ++e)
-          b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
-        y = vadd(x, b);
-      }
-      uint16_t* dst = C + row * ldc + c0;
-      if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
-        store_out_vec<kHalfOut, VEC>(dst, y);
-      } else {
-#pragma unroll
-        for (int e = 0; e < VEC; ++e)
-          if (j + e < bn && c0 + e < N) dst[e] = round_out<kHalfOut>(y.v[e]);
-      }
-    };
-    Prog::template run<VecF<VEC>>(in, out);
+    recombine_vector<Prog, S, VEC, kHalfOut>(raw, i, j, bm, bn, bias, C, M, N, ldc, vector_stores);
   }
 }
 
