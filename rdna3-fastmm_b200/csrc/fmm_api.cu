@@ -155,7 +155,7 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
   static constexpr int S = 4;
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
-  static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 16;
+  static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 64;
 };
 
 int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int blocks_per_sm) {
