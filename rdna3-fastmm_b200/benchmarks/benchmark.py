@@ -15,6 +15,8 @@ round; correctness compares a centred tile of every output macroblock with a
 CPU FP32 product of the original inputs.  ``--linear-implementation op`` (the
 reference's ``triton-op``) times the allocating ``torch.ops.rdna3_fastmm``
 operator; ``plan`` times ``run_linear`` with a preallocated workspace.
+``--sustained-seconds S`` (B200 addition) times each operation as a
+back-to-back loop of about S seconds, the regime a power-capped GPU settles in.
 """
 
 from __future__ import annotations
@@ -135,8 +137,20 @@ def timed_ms(operation: Callable[[], None]) -> float:
     return float(begin.elapsed_time(end))
 
 
-def measure_operations(operations: dict, warmups: int, rounds: int):
-    """Every operation once per round, the starting operation rotating."""
+def loop_count(single_ms: float, sustained_seconds: float) -> int:
+    """Calls in one sustained measurement: enough to last ``sustained_seconds``."""
+    return max(1, round(sustained_seconds * 1e3 / max(single_ms, 1e-3)))
+
+
+def measure_operations(operations: dict, warmups: int, rounds: int, sustained_seconds: float = 0.0):
+    """Every operation once per round, the starting operation rotating.
+
+    With ``sustained_seconds > 0`` each measurement is instead one event pair
+    around a back-to-back loop lasting about that long, divided by the call
+    count: on a power-capped part a single call is timed at whatever clock the
+    previous operation left, while the loop reaches the steady clock that
+    operation sustains on its own.
+    """
     names = list(operations)
 
     def rotated(k: int) -> list:
@@ -147,14 +161,35 @@ def measure_operations(operations: dict, warmups: int, rounds: int):
         for name in rotated(w):
             operations[name]()
     torch.cuda.synchronize()
+    counts = dict.fromkeys(names, 1)
+    if sustained_seconds > 0:
+        counts = {n: loop_count(timed_ms(operations[n]), sustained_seconds) for n in names}
+
+    def measured(name: str) -> float:
+        op, n = operations[name], counts[name]
+        if n == 1:
+            return timed_ms(op)
+
+        def loop():
+            for _ in range(n):
+                op()
+        return timed_ms(loop) / n
+
     raw = {name: [] for name in names}
     schedule = []
     for r in range(rounds):
         order = rotated(r)
         schedule.append(order)
         for name in order:
-            raw[name].append(timed_ms(operations[name]))
+            raw[name].append(measured(name))
     return {name: summarize(v) for name, v in raw.items()}, schedule
+
+
+def timing_method(sustained_seconds: float) -> str:
+    if sustained_seconds > 0:
+        return (f"one CUDA event pair around a back-to-back loop of about {sustained_seconds:g} s "
+                "per operation, divided by the call count")
+    return "one operation per CUDA event pair"
 
 
 def macroblock_tile_starts(dimension: int, tile: int, scheme_size: int) -> list:
@@ -278,7 +313,7 @@ def algorithm_metrics(timings: dict, shape, plan, operator: str, baseline: str, 
 def benchmark(algorithm: str, shape, dtype, compute_dtype, modes, warmups: int, rounds: int,
               tile_size: int, seed: int, max_memory_fraction: float, allow_dirty: bool,
               allow_unrecommended: bool, operator: str = "mm", linear_bias: bool = True,
-              linear_implementation: str = "op") -> dict:
+              linear_implementation: str = "op", sustained_seconds: float = 0.0) -> dict:
     commit, dirty = tree_state()
     require_clean(dirty, allow_dirty)
     if operator not in ("mm", "linear"):
@@ -370,7 +405,7 @@ def benchmark(algorithm: str, shape, dtype, compute_dtype, modes, warmups: int, 
                 plan.run_packed(left, packed, pws, outputs["candidate_prepacked"])
         operations["candidate_prepacked"] = run_prepacked
     with torch.no_grad():
-        timings, schedule = measure_operations(operations, warmups, rounds)
+        timings, schedule = measure_operations(operations, warmups, rounds, sustained_seconds)
     torch.cuda.synchronize()
     correctness = validate_outputs(left, right, bias, outputs, baseline, tile_size, plan.scheme_size)
     algorithms = algorithm_metrics(timings, shape, plan, operator, baseline, linear_implementation)
@@ -413,7 +448,7 @@ def benchmark(algorithm: str, shape, dtype, compute_dtype, modes, warmups: int, 
             "seed": seed, "input_distribution": f"independent standard normal rounded to {dname}",
             "input_output_dtype": dname, "compute_dtype": cname, "warmup_rounds": warmups,
             "measured_rounds": rounds, "order_schedule": schedule,
-            "timing_method": "one operation per CUDA event pair", "operator": operator,
+            "timing_method": timing_method(sustained_seconds), "operator": operator,
             "weight_layout": "out_in" if operator == "linear" else "inner_columns",
             "bias": bias is not None,
             "correctness_reference": "CPU FP32 tile matmul from original inputs"
@@ -449,6 +484,8 @@ def main(argv=None) -> None:
     parser.add_argument("--mode", choices=("dynamic", "prepacked", "external", "both"), default="both")
     parser.add_argument("--warmups", type=int, default=3)
     parser.add_argument("--rounds", type=int, default=9)
+    parser.add_argument("--sustained-seconds", type=float, default=0.0,
+                        help="time each operation as a back-to-back loop of about this long")
     parser.add_argument("--tile-size", type=int, default=16)
     parser.add_argument("--seed", type=int, default=0)
     parser.add_argument("--max-memory-fraction", type=float, default=0.75)
@@ -460,6 +497,8 @@ def main(argv=None) -> None:
         parser.error("warmups must be positive and rounds must be at least three")
     if args.tile_size < 1:
         parser.error("tile size must be positive")
+    if args.sustained_seconds < 0:
+        parser.error("sustained seconds must not be negative")
     if args.no_bias and args.operator != "linear":
         parser.error("--no-bias requires --operator linear")
     if not 0 < args.max_memory_fraction <= 1:
@@ -471,7 +510,7 @@ def main(argv=None) -> None:
     report = benchmark(args.algorithm, args.shape, dtype, compute, modes, args.warmups, args.rounds,
                        args.tile_size, args.seed, args.max_memory_fraction, args.allow_dirty,
                        args.allow_unrecommended, args.operator, not args.no_bias,
-                       args.linear_implementation)
+                       args.linear_implementation, args.sustained_seconds)
     text = json.dumps(report, indent=2, allow_nan=False) + "\n"
     if args.output is None:
         print(text, end="")

@@ -29,7 +29,8 @@ if __package__ in (None, ""):
 
 from benchmarks.benchmark import (  # noqa: E402
     ARTIFACTS, ENVIRONMENT_KEYS, GENERATED_HEADER, PACKAGE_ROOT, file_sha256, measure_operations,
-    measure_packing, packing_break_even_reuses, parse_shape, require_clean, tree_state, validate_outputs,
+    measure_packing, packing_break_even_reuses, parse_shape, require_clean, timing_method, tree_state,
+    validate_outputs,
 )
 from rdna3_fastmm import _native  # noqa: E402
 from rdna3_fastmm.runtime import Rank48Plan  # noqa: E402
@@ -67,7 +68,7 @@ def status(timings: dict) -> tuple[str, str, float]:
 
 
 def benchmark(shape, warmups: int, rounds: int, tile_size: int, seed: int, max_memory_fraction: float,
-              allow_dirty: bool, allow_unrecommended: bool) -> dict:
+              allow_dirty: bool, allow_unrecommended: bool, sustained_seconds: float = 0.0) -> dict:
     commit, dirty = tree_state()
     require_clean(dirty, allow_dirty)
     device = torch.device("cuda", torch.cuda.current_device())
@@ -100,7 +101,7 @@ def benchmark(shape, warmups: int, rounds: int, tile_size: int, seed: int, max_m
     for n, plan in plans.items():
         operations[n] = (lambda plan=plan, n=n: plan.run_linear_packed(
             x, packed[n], workspaces[n], output=outputs[n]))
-    timings, order = measure_operations(operations, warmups, rounds)
+    timings, order = measure_operations(operations, warmups, rounds, sustained_seconds)
     correctness = validate_outputs(x, weight.T, None, outputs, "torch_bfloat16", tile_size,
                                    Rank48Plan.scheme_size)
     native_ms = timings["torch_bfloat16"].median_ms
@@ -134,7 +135,7 @@ def benchmark(shape, warmups: int, rounds: int, tile_size: int, seed: int, max_m
         "protocol": {
             "shape": list(shape), "source_dtype": "bfloat16", "compute_dtype": "float16", "bias": False,
             "warmup_rounds": warmups, "measured_rounds": rounds, "order_schedule": order,
-            "timing_method": "one operation per CUDA event pair",
+            "timing_method": timing_method(sustained_seconds),
             "allocation_contract": "all hot-path operations reuse output buffers; reduced-rank plans "
                                    "also reuse their prepacked weights and workspaces",
             "correctness_reference": "CPU FP32 tiles from original BF16 inputs",
@@ -167,6 +168,8 @@ def main(argv=None) -> None:
     parser.add_argument("--shape", type=parse_shape, required=True)
     parser.add_argument("--warmups", type=int, default=1)
     parser.add_argument("--rounds", type=int, default=7)
+    parser.add_argument("--sustained-seconds", type=float, default=0.0,
+                        help="time each operation as a back-to-back loop of about this long")
     parser.add_argument("--tile-size", type=int, default=8)
     parser.add_argument("--seed", type=int, default=0)
     parser.add_argument("--max-memory-fraction", type=float, default=0.5)
@@ -179,11 +182,14 @@ def main(argv=None) -> None:
         parser.error("warmups must be positive and rounds must be at least three")
     if args.tile_size < 1:
         parser.error("tile size must be positive")
+    if args.sustained_seconds < 0:
+        parser.error("sustained seconds must not be negative")
     if not 0 < args.max_memory_fraction <= 1:
         parser.error("max memory fraction must be in the interval (0, 1]")
     torch.set_grad_enabled(False)
     report = benchmark(args.shape, args.warmups, args.rounds, args.tile_size, args.seed,
-                       args.max_memory_fraction, args.allow_dirty, args.allow_unrecommended)
+                       args.max_memory_fraction, args.allow_dirty, args.allow_unrecommended,
+                       args.sustained_seconds)
     text = json.dumps(report, indent=2, allow_nan=False) + "\n"
     if args.output is None:
         print(text, end="")

@@ -147,6 +147,14 @@ def test_packing_break_even_reuses():
     assert harness.packing_break_even_reuses(10.0, 1.0, 2.0) is None
 
 
+def test_sustained_loop_count_and_method():
+    assert harness.loop_count(2.0, 1.0) == 500
+    assert harness.loop_count(5000.0, 1.0) == 1
+    assert harness.loop_count(0.0, 0.5) == 500000
+    assert harness.timing_method(0.0) == "one operation per CUDA event pair"
+    assert "1.5 s" in harness.timing_method(1.5)
+
+
 def test_macroblock_tile_starts_are_centred():
     assert harness.macroblock_tile_starts(64, 8, 2) == [12, 44]
     assert harness.macroblock_tile_starts(11, 2, 4) == [0, 3, 6, 9]
@@ -220,8 +228,9 @@ def test_report_on_b200(algorithm, operator, implementation, modes, dtype):
 def test_compare_prepacked_linear_on_b200():
     from benchmarks import compare_prepacked_linear as compare
 
-    report = compare.benchmark((520, 384, 264), 1, 3, 8, 0, 0.5, True, True)
+    report = compare.benchmark((520, 384, 264), 1, 3, 8, 0, 0.5, True, True, sustained_seconds=0.02)
     json.dumps(report, allow_nan=False)
+    assert "loop" in report["protocol"]["timing_method"]
     assert report["status"] in ("rank48-wins", "rank48-does-not-beat-current-control")
     assert set(report["case"]["timings"]) == {"torch_bfloat16", "rank7", "rank49", "rank48"}
     for name in ("rank7", "rank48"):
