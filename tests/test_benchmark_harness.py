@@ -255,3 +255,18 @@ def test_compare_status_picks_fastest_control():
     assert compare.status(t) == ("rank48-wins", "rank49", 1.5)
     t["rank48"] = harness.summarize([1.6, 1.6, 1.6])
     assert compare.status(t)[0] == "rank48-does-not-beat-current-control"
+
+
+MODEL_SHAPES = DEFAULT_CORPUS_PATH.parent / "model-shapes.json"
+
+
+def test_model_shape_corpus_matches_reference_case_ids():
+    corpus = load_corpus(MODEL_SHAPES)
+    assert len(corpus.cases) == 15 and len({c.id for c in corpus.cases}) == 15
+    assert {c.model for c in corpus.cases} >= {"HiDream-O1", "Ideogram 4", "LTX-2.3", "Qwen-Image-Edit-2511"}
+    assert all(c.input_output_dtype == "bfloat16" and c.compute_dtype == "float16" for c in corpus.cases)
+    assert corpus.case("ltx-2.3-blueprint-4992-mlp-up").shape == (4992, 4096, 16384)
+    assert corpus.case("ltx-2.3-blueprint-4992-mlp-down").shape == (4992, 16384, 4096)
+    case = corpus.case("ideogram4-local-8214-mlp-up")
+    command = benchmark_command(case, _config(), Path("results/case.json"))
+    assert command[command.index("--shape") + 1] == "8214,4608,12288" and "--no-bias" in command
