@@ -48,6 +48,8 @@ typedef struct CUstream_st* fmm_stream_t; /* == cudaStream_t */
 #define FMM_SCHEME_RANK7 7   /* <2,2,2> rank 7 (Strassen-Winograd form)  */
 #define FMM_SCHEME_RANK48 48 /* <4,4,4> rank 48 dyadic-rational SLP        */
 #define FMM_SCHEME_RANK49 49 /* <4,4,4> rank 49 (rank 7 (x) rank 7)        */
+#define FMM_SCHEME_RANK343 343 /* <8,8,8> rank 343, FP16 only (reference     */
+                               /* Rank343Plan, runtime.py:883-962)          */
 
 /* bits of the device status word */
 #define FMM_STATUS_TIMEOUT 1u

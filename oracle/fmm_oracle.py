@@ -19,7 +19,9 @@ It restates, in numpy, the algorithm of chelokot/rdna3-fastmm for one
 4. leaf products ``P_r = L_r @ R_r`` accumulated wide and stored FP16
    (``torch.bmm`` at ``src/rdna3_fastmm/runtime.py:728-732``);
 5. output transform ``C_o = sum_r W[o,r] P_r (+ bias)`` in FP32 with a BF16
-   round-to-nearest-even store (``output_transform{,_bias}_kernel``).
+   round-to-nearest-even store (``output_transform{,_bias}_kernel``); for the
+   FP16 square rank-343 scheme, a +-1 coefficient sum with an FP16 store
+   (``generated/rank343_8x8x8.py`` ``output_transform_mfma_kernel``).
 
 Every gate and output is evaluated with the association written in the
 certificate (left to right over signed terms for reduced circuits, the parsed
@@ -46,7 +48,12 @@ SCHEMES = {
     "rank7": ("reduced", "2x2x2_rank7_15add", 2, 7),
     "rank49": ("reduced", "4x4x4_rank49_159add", 4, 49),
     "rank48": ("slp", "4x4x4_rank48_accurate", 4, 48),
+    "rank343": ("reduced", "8x8x8_rank343_1661add", 8, 343),
 }
+# schemes whose output side is a +-1 coefficient sum rather than the circuit
+# (the reference reconstructs rank 343 with a matrix product against the
+# expanded coefficients: generated/rank343_8x8x8.py output_transform_mfma_kernel)
+COEFFICIENT_SUM_OUTPUT = frozenset({"rank343"})
 
 
 # ---------------------------------------------------------------- number formats
@@ -191,13 +198,39 @@ def leaf_products(L: np.ndarray, R: np.ndarray) -> np.ndarray:
     return np.matmul(L.astype(np.float64), R.astype(np.float64)).astype(np.float16)
 
 
+@lru_cache(maxsize=None)
+def output_coefficients(name: str) -> np.ndarray:
+    """Expanded output map W[o, r] (row-major C blocks), exact integers: the
+    output circuit evaluated on unit vectors."""
+    s, rank, _, _, output = scheme_circuits(name)
+    units = [np.eye(rank, dtype=np.float64)[r] for r in range(rank)]
+    return np.stack(output.evaluate(units)).astype(np.int64)
+
+
+def _coefficient_sum(name: str, P: np.ndarray) -> list[np.ndarray]:
+    """``C_o = sum_r W[o, r] P_r`` accumulated in float32 from +0 in ascending
+    r, one add or subtract per +-1 coefficient (the order the B200 kernel
+    uses; the reference's matrix-product reconstruction leaves the order to
+    the hardware)."""
+    W = output_coefficients(name)
+    acc = [np.zeros(P.shape[1:], dtype=np.float32) for _ in range(W.shape[0])]
+    for r in range(W.shape[1]):
+        p = P[r].astype(np.float32)
+        for o in np.nonzero(W[:, r])[0]:
+            acc[o] = acc[o] + p if W[o, r] > 0 else acc[o] - p
+    return acc
+
+
 def output_transform(name: str, P: np.ndarray, M: int, N: int,
                      bias: np.ndarray | None = None, out_dtype: str = "bf16") -> np.ndarray:
     """P [R, bm, bn] float16 -> C [M, N] as float32 holding bf16 values
     (``out_dtype="fp16"``: FP16 values, the reference's FP16-plan output)."""
     s, rank, _, _, output = scheme_circuits(name)
     bm, bn = P.shape[1], P.shape[2]
-    outs = output.evaluate([P[r].astype(np.float32) for r in range(rank)])
+    if name in COEFFICIENT_SUM_OUTPUT:
+        outs = _coefficient_sum(name, P)
+    else:
+        outs = output.evaluate([P[r].astype(np.float32) for r in range(rank)])
     C = np.zeros((s * bm, s * bn), dtype=np.float32)
     for o, value in enumerate(outs):
         br, bc = divmod(o, s)
@@ -218,6 +251,18 @@ def linear(name: str, A: np.ndarray, W: np.ndarray, bias: np.ndarray | None = No
     R = weight_transform(name, W)
     P = products(L, R)
     return output_transform(name, P, A.shape[0], W.shape[0], bias)
+
+
+def right_transform(name: str, B: np.ndarray) -> np.ndarray:
+    """B [K, N] (the plain-mm right operand) -> R [R, bk, bn] float16."""
+    return weight_transform(name, np.ascontiguousarray(np.asarray(B, dtype=np.float32).T))
+
+
+def matmul(name: str, A: np.ndarray, B: np.ndarray, products=leaf_products) -> np.ndarray:
+    """Plain ``A @ B`` with FP16 inputs and output (the mm API)."""
+    L = left_transform(name, A)
+    R = right_transform(name, B)
+    return output_transform(name, products(L, R), A.shape[0], B.shape[1], None, "fp16")
 
 
 def relative_l2(candidate: np.ndarray, reference: np.ndarray) -> float:

@@ -45,7 +45,9 @@ if str(PACKAGE_ROOT) not in sys.path:
 from rdna3_fastmm import _native  # noqa: E402
 from rdna3_fastmm.external_mm import rdna3_rank49_dynamic_v1_out  # noqa: E402
 from rdna3_fastmm.linear import rdna3_linear, rdna3_rank7_linear, rdna3_rank48_linear  # noqa: E402
-from rdna3_fastmm.runtime import PackedRight, PackedWeight, Rank7Plan, Rank48Plan, Rank49Plan  # noqa: E402
+from rdna3_fastmm.runtime import (  # noqa: E402
+    PackedRight, PackedWeight, Rank7Plan, Rank48Plan, Rank49Plan, Rank343Plan,
+)
 from rdna3_fastmm.schemes import CERTIFICATE_ROOT  # noqa: E402
 
 GENERATED_HEADER = PACKAGE_ROOT / "csrc" / "generated" / "fmm_schemes.cuh"
@@ -54,9 +56,10 @@ ARTIFACTS = {
     "rank49": (CERTIFICATE_ROOT / "4x4x4_rank49_159add" / "certificate.json", Rank49Plan, rdna3_linear),
     "rank48": (CERTIFICATE_ROOT / "4x4x4_rank48_accurate" / "certificate.json", Rank48Plan,
                rdna3_rank48_linear),
+    "rank343": (CERTIFICATE_ROOT / "8x8x8_rank343_1661add" / "certificate.json", Rank343Plan, None),
 }
 OPERATOR_NAMES = {"rank7": "rdna3_fastmm::linear_rank7", "rank49": "rdna3_fastmm::linear",
-                  "rank48": "rdna3_fastmm::linear_rank48"}
+                  "rank48": "rdna3_fastmm::linear_rank48", "rank343": "(none)"}
 DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16}
 ENVIRONMENT_KEYS = ("CUDA_VISIBLE_DEVICES", "CUBLAS_WORKSPACE_CONFIG", "NCCL_DEBUG",
                     "FMM_LEAF_GEMM_VARIANT", "PYTORCH_CUDA_ALLOC_CONF")
@@ -326,6 +329,8 @@ def benchmark(algorithm: str, shape, dtype, compute_dtype, modes, warmups: int, 
         raise ValueError("linear benchmarking supports dynamic and prepacked modes")
     if operator == "linear" and "prepacked" in modes and linear_implementation != "plan":
         raise ValueError("prepacked Linear benchmarking requires the plan implementation")
+    if algorithm == "rank343" and operator != "mm":
+        raise ValueError("rank 343 is a plain-mm (FP16) scheme")
     device = torch.device("cuda", torch.cuda.current_device())
     certificate, plan_type, operator_fn = ARTIFACTS[algorithm]
     plan = plan_type(*shape, device=device, dtype=dtype, compute_dtype=compute_dtype)

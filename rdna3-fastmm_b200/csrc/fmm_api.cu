@@ -52,6 +52,7 @@ int scheme_size(int scheme) {
     case FMM_SCHEME_RANK7: return 2;
     case FMM_SCHEME_RANK48: return 4;
     case FMM_SCHEME_RANK49: return 4;
+    case FMM_SCHEME_RANK343: return 8;
     default: return 0;
   }
 }
@@ -136,6 +137,8 @@ struct SchemeTraits<FMM_SCHEME_RANK7> {
   static constexpr int VEC = 8;
   static constexpr int kInThreads = 256, kInBlocks = 1, kInGrid = 64;
   static constexpr int kOutVec = 8, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 64;
+  static constexpr bool kSumOutput = false;
+  static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK48> {
@@ -146,6 +149,8 @@ struct SchemeTraits<FMM_SCHEME_RANK48> {
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 16;
+  static constexpr bool kSumOutput = false;
+  static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK49> {
@@ -156,6 +161,24 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 64;
+  static constexpr bool kSumOutput = false;
+  static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
+};
+// Rank 343: 64 inputs and 343 planes per position.  The input side keeps two
+// elements per thread (64 packed inputs plus the circuit fit in registers);
+// the output side is the +-1 coefficient sum with 64 accumulators of two
+// elements; the K x N right transform stages 64 tiles of 16 x 16.
+template <>
+struct SchemeTraits<FMM_SCHEME_RANK343> {
+  using Left = gen::Rank343Left;
+  using Right = gen::Rank343Right;
+  using Output = gen::Rank343OutputSum;
+  static constexpr int S = 8;
+  static constexpr int VEC = 2;
+  static constexpr int kInThreads = 128, kInBlocks = 1, kInGrid = 16;
+  static constexpr int kOutVec = 2, kOutThreads = 128, kOutBlocks = 1, kOutGrid = 16;
+  static constexpr bool kSumOutput = true;
+  static constexpr int kKnTile = 16, kKnVec = 2, kKnThreads = 128;
 };
 
 int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int blocks_per_sm) {
@@ -191,10 +214,18 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
   if (int rc = device_info(&info)) return rc;
   const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
   const int64_t items = d.bm * ceil_div(d.bn, V);
-  reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
-      <<<streaming_grid(info, items, T::kOutThreads, T::kOutGrid), T::kOutThreads, 0, stream>>>(
-          static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
-          static_cast<uint16_t*>(C), M, N, ldc, vec ? 1 : 0);
+  const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
+  if constexpr (T::kSumOutput) {
+    reconstruct_sum_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
+        <<<grid, T::kOutThreads, 0, stream>>>(
+            static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
+            static_cast<uint16_t*>(C), M, N, ldc, vec ? 1 : 0);
+  } else {
+    reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
+        <<<grid, T::kOutThreads, 0, stream>>>(
+            static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
+            static_cast<uint16_t*>(C), M, N, ldc, vec ? 1 : 0);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
   return FMM_OK;
@@ -204,11 +235,12 @@ template <int SCHEME, bool kHalf>
 int launch_right_kn(const void* B, int64_t K, int64_t N, int64_t ldb, void* dst, const fmm_dims& d,
                     cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
-  constexpr int kTile = 32;
+  constexpr int kTile = T::kKnTile;
   const dim3 grid(static_cast<unsigned>(ceil_div(d.ldk, kTile)),
                   static_cast<unsigned>(ceil_div(d.bn, kTile)));
-  right_transform_kn_kernel<typename T::Right, T::S, kHalf, kTile><<<grid, 256, 0, stream>>>(
-      static_cast<const uint16_t*>(B), K, N, ldb, static_cast<__half*>(dst), d.bk, d.bn, d.ldk);
+  right_transform_kn_kernel<typename T::Right, T::S, kHalf, kTile, T::kKnVec>
+      <<<grid, T::kKnThreads, 0, stream>>>(static_cast<const uint16_t*>(B), K, N, ldb,
+                                           static_cast<__half*>(dst), d.bk, d.bn, d.ldk);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "right transform (K x N) launch");
   return FMM_OK;
@@ -223,6 +255,10 @@ int dispatch(int scheme, int dtype, Args... args) {
       return half ? F<FMM_SCHEME_RANK7, true>::run(args...) : F<FMM_SCHEME_RANK7, false>::run(args...);
     case FMM_SCHEME_RANK48:
       return half ? F<FMM_SCHEME_RANK48, true>::run(args...) : F<FMM_SCHEME_RANK48, false>::run(args...);
+    case FMM_SCHEME_RANK343:
+      // FP16 inputs and output only, as the reference plan (precision_pairs)
+      if (!half) return fail(FMM_ERR_UNSUPPORTED, "rank 343 takes FP16 operands only");
+      return F<FMM_SCHEME_RANK343, true>::run(args...);
     default:
       return half ? F<FMM_SCHEME_RANK49, true>::run(args...) : F<FMM_SCHEME_RANK49, false>::run(args...);
   }

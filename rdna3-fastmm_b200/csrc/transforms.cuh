@@ -225,6 +225,36 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
 // recombination, then rounded to nearest even (BF16 or FP16).  `raw` holds the
 // R product vectors, already loaded.  Shared by the reconstruct kernel and the
 // fused rank-7 epilogue of the leaf GEMM, so both round identically.
+// Store output o (C block (o / S, o % S)) of one vector position: optional
+// bias, then one rounding to the output format; ragged edges element-wise.
+template <int S, int VEC, bool kHalfOut>
+__device__ __forceinline__ void store_output_vector(int o, const VecF<VEC>& x, int64_t i, int64_t j,
+                                                    int64_t bm, int64_t bn,
+                                                    const uint16_t* __restrict__ bias,
+                                                    uint16_t* __restrict__ C, int64_t M, int64_t N,
+                                                    int64_t ldc, int vector_stores) {
+  const int br = o / S, bc = o % S;
+  const int64_t row = br * bm + i;
+  if (row >= M) return;
+  const int64_t c0 = bc * bn + j;
+  VecF<VEC> y = x;
+  if (bias != nullptr) {
+    VecF<VEC> b;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e)
+      b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
+    y = vadd(x, b);
+  }
+  uint16_t* dst = C + row * ldc + c0;
+  if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
+    store_out_vec<kHalfOut, VEC>(dst, y);
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e)
+      if (j + e < bn && c0 + e < N) dst[e] = round_out<kHalfOut>(y.v[e]);
+  }
+}
+
 template <class Prog, int S, int VEC, bool kHalfOut>
 __device__ __forceinline__ void recombine_vector(const typename VecIO<VEC>::H (&raw)[Prog::kInputs],
                                                  int64_t i, int64_t j, int64_t bm, int64_t bn,
@@ -233,26 +263,7 @@ __device__ __forceinline__ void recombine_vector(const typename VecIO<VEC>::H (&
                                                  int64_t ldc, int vector_stores) {
   auto in = [&](int r) -> VecF<VEC> { return unpack_half<VEC>(raw[r]); };
   auto out = [&](int o, const VecF<VEC>& x) {
-    const int br = o / S, bc = o % S;
-    const int64_t row = br * bm + i;
-    if (row >= M) return;
-    const int64_t c0 = bc * bn + j;
-    VecF<VEC> y = x;
-    if (bias != nullptr) {
-      VecF<VEC> b;
-#pragma unroll
-      for (int e = 0; e < VEC; ++e)
-        b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
-      y = vadd(x, b);
-    }
-    uint16_t* dst = C + row * ldc + c0;
-    if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
-      store_out_vec<kHalfOut, VEC>(dst, y);
-    } else {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e)
-        if (j + e < bn && c0 + e < N) dst[e] = round_out<kHalfOut>(y.v[e]);
-    }
+    store_output_vector<S, VEC, kHalfOut>(o, x, i, j, bm, bn, bias, C, M, N, ldc, vector_stores);
   };
   Prog::template run<VecF<VEC>>(in, out);
 }
@@ -277,6 +288,41 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
     for (int r = 0; r < Prog::kInputs; ++r)
       raw[r] = __ldg(reinterpret_cast<const Raw*>(P + r * plane + static_cast<int64_t>(i) * ldp + j));
     recombine_vector<Prog, S, VEC, kHalfOut>(raw, i, j, bm, bn, bias, C, M, N, ldc, vector_stores);
+  }
+}
+
+// Output side as a +-1 coefficient sum (``Prog::accumulate``), for schemes
+// whose product count is too large to keep every product of a position in
+// registers (rank 343): each thread owns VEC consecutive plane columns and
+// Prog::kOutputs FP32 accumulators starting at +0; the generated code reads
+// the products a group at a time, in ascending order, and adds or subtracts
+// each into the outputs it feeds.
+template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = true>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_sum_kernel(
+    const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
+    const uint16_t* __restrict__ bias, uint16_t* __restrict__ C, int64_t M, int64_t N,
+    int64_t ldc, int vector_stores) {
+  using Raw = typename VecIO<VEC>::H;
+  const int64_t plane = bm * ldp;
+  const uint32_t vecs_per_row = static_cast<uint32_t>((bn + VEC - 1) / VEC);
+  const uint32_t total = static_cast<uint32_t>(bm) * vecs_per_row;
+  for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += gridDim.x * blockDim.x) {
+    const uint32_t i = idx / vecs_per_row;
+    const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
+    const __half* base = P + static_cast<int64_t>(i) * ldp + j;
+    VecF<VEC> acc[Prog::kOutputs];
+#pragma unroll
+    for (int o = 0; o < Prog::kOutputs; ++o)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[o].v[e] = 0.0f;
+    auto in = [&](int r) -> VecF<VEC> {
+      return unpack_half<VEC>(__ldg(reinterpret_cast<const Raw*>(base + r * plane)));
+    };
+    Prog::template accumulate<VecF<VEC>>(in, acc);
+#pragma unroll
+    for (int o = 0; o < Prog::kOutputs; ++o)
+      store_output_vector<S, VEC, kHalfOut>(o, acc[o], i, j, bm, bn, bias, C, M, N, ldc, vector_stores);
   }
 }
 

@@ -26,7 +26,7 @@ FMM_RIGHT_KN = 2
 FMM_DTYPE_BF16 = 0
 FMM_DTYPE_F16 = 1
 
-SCHEME_IDS = {"rank7": 7, "rank48": 48, "rank49": 49}
+SCHEME_IDS = {"rank7": 7, "rank48": 48, "rank49": 49, "rank343": 343}
 
 
 class NativeLibraryError(RuntimeError):

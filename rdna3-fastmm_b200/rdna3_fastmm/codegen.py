@@ -8,7 +8,7 @@ kernels (``csrc/transforms.cuh``); the generated part only fixes *which*
 signals are combined and *in what order*, one ``vadd``/``vsub``/``vneg``/
 ``vscale`` per certificate operation, so that each FP32 rounding happens
 exactly where the reference's generated kernels round
-(``src/rdna3_fastmm/generated/rank{7_2x2x2,48_4x4x4,49_4x4x4}.py``).
+(``src/rdna3_fastmm/generated/rank{7_2x2x2,48_4x4x4,49_4x4x4,343_8x8x8}.py``).
 
 The output file is checked in; ``tests/test_codegen.py`` regenerates it and
 requires byte equality, like the reference's own generator-determinism tests
@@ -23,7 +23,7 @@ from fractions import Fraction
 from pathlib import Path
 
 from .program import Expr, LinearProgram, expr_signals
-from .schemes import SCHEME_NAMES, get_scheme
+from .schemes import SCHEME_NAMES, SQUARE_SCHEME_NAMES, get_scheme
 
 GENERATED_HEADER = (
     Path(__file__).resolve().parent.parent / "csrc" / "generated" / "fmm_schemes.cuh"
@@ -83,6 +83,47 @@ def _struct(name: str, program: LinearProgram) -> str:
     )
 
 
+def _output_sum_struct(name: str, program: LinearProgram, group: int = 8) -> str:
+    """Output side as a coefficient sum: ``acc[o] += W[o][r] * p_r`` for r in
+    ascending order, one FP32 add or subtract per nonzero (all coefficients
+    are +-1).  Used where the product count makes a register-resident circuit
+    impractical (rank 343: 343 inputs, 527 gates); the reference reconstructs
+    this scheme with a tensor-core product against the same coefficient
+    matrix, whose summation order is unspecified, so parity for this side is
+    by tolerance.  Products are read ``group`` at a time so their loads are
+    in flight together."""
+    rows = program.coefficients()
+    columns: list[list[tuple[int, int]]] = [[] for _ in range(program.inputs)]
+    for o, row in enumerate(rows):
+        for r, c in enumerate(row):
+            if c == 0:
+                continue
+            if c not in (1, -1):
+                raise ValueError("the coefficient-sum output needs +-1 coefficients")
+            columns[r].append((o, int(c)))
+    body: list[str] = []
+    for start in range(0, program.inputs, group):
+        stop = min(start + group, program.inputs)
+        body.append("    {")
+        for r in range(start, stop):
+            body.append(f"      const V p{r} = in({r});")
+        for r in range(start, stop):
+            for o, c in columns[r]:
+                op = "vadd" if c > 0 else "vsub"
+                body.append(f"      acc[{o}] = {op}(acc[{o}], p{r});")
+        body.append("    }")
+    return (
+        f"struct {name} {{\n"
+        f"  static constexpr int kInputs = {program.inputs};\n"
+        f"  static constexpr int kOutputs = {program.outputs};\n"
+        f"  template <class V, class In>\n"
+        f"  static __device__ __forceinline__ void accumulate(const In& in, V (&acc)[{program.outputs}]) {{\n"
+        + "\n".join(body) + "\n"
+        f"  }}\n"
+        f"}};\n"
+    )
+
+
 def generate() -> str:
     parts = [
         "// Generated by rdna3_fastmm/codegen.py from the vendored certificates.",
@@ -97,7 +138,7 @@ def generate() -> str:
         "namespace gen {",
         "",
     ]
-    for name in SCHEME_NAMES:
+    for name in SCHEME_NAMES + SQUARE_SCHEME_NAMES:
         scheme = get_scheme(name)
         camel = name.capitalize()
         parts.append(f"// {scheme.algorithm}: <{scheme.size},{scheme.size},{scheme.size}> rank {scheme.rank}")
@@ -107,7 +148,10 @@ def generate() -> str:
         parts.append("")
         parts.append(_struct(f"{camel}Left", scheme.left))
         parts.append(_struct(f"{camel}Right", scheme.right))
-        parts.append(_struct(f"{camel}Output", scheme.output))
+        if name in SQUARE_SCHEME_NAMES:
+            parts.append(_output_sum_struct(f"{camel}OutputSum", scheme.output))
+        else:
+            parts.append(_struct(f"{camel}Output", scheme.output))
     parts.append("}  // namespace gen")
     parts.append("}  // namespace fmm")
     return "\n".join(parts) + "\n"

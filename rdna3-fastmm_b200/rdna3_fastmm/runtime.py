@@ -37,6 +37,7 @@ __all__ = [
     "ElementTransformConfig",
     "WeightTransformConfig",
     "Rank7Plan",
+    "Rank343Plan",
     "Rank48Plan",
     "Rank49Plan",
     "Rank7Workspace",
@@ -526,7 +527,25 @@ class Rank49Plan(_LinearPlan):
     prepacked_linear_shape_families: tuple[LinearShapeFamily, ...] = ()
 
 
-for _plan in (Rank7Plan, Rank48Plan, Rank49Plan):
+class Rank343Plan(_LinearPlan):
+    """``<8,8,8>`` rank-343 scheme for FP16 square products
+    (reference ``runtime.py:883-962``): FP16 inputs and output only, the
+    plain-mm API (``run``, ``pack_right``, ``run_packed``).  The output side is
+    the +-1 coefficient sum over the 343 products (the reference uses a matrix
+    product against the same coefficients).  No shape is admitted by
+    ``is_recommended`` until one measures faster than cuBLAS FP16 on B200."""
+
+    algorithm = "rank343-mfma-v1"
+    scheme = "rank343"
+    rank = 343
+    scheme_size = 8
+    precision_pairs = frozenset({(torch.float16, torch.float16)})
+    transform_vector = 2
+    dynamic_shapes: frozenset = frozenset()
+    prepacked_shapes: frozenset = frozenset()
+
+
+for _plan in (Rank7Plan, Rank48Plan, Rank49Plan, Rank343Plan):
     _scheme = get_scheme(_plan.scheme)
     assert (_scheme.rank, _scheme.size) == (_plan.rank, _plan.scheme_size), _plan
 

@@ -1,4 +1,4 @@
-"""The three verified block schemes on the fast path, as linear programs.
+"""The verified block schemes on the fast path, as linear programs.
 
 Every scheme is loaded from its vendored certificate and verified exactly on
 every load (integer Brent tensor for reduced circuits, Fraction Brent tensor
@@ -32,7 +32,7 @@ from .slp import load_and_verify_slp_certificate
 
 CERTIFICATE_ROOT = Path(__file__).resolve().parent / "certificates"
 
-__all__ = ["Scheme", "get_scheme", "SCHEME_NAMES", "CERTIFICATE_ROOT"]
+__all__ = ["Scheme", "get_scheme", "SCHEME_NAMES", "SQUARE_SCHEME_NAMES", "CERTIFICATE_ROOT"]
 
 
 @dataclass(frozen=True)
@@ -111,12 +111,15 @@ def _slp_scheme(name: str, algorithm: str, folder: str) -> Scheme:
 
 
 SCHEME_NAMES = ("rank7", "rank48", "rank49")
+# FP16 square plain-mm scheme (reference ``Rank343Plan``, ``runtime.py:883-962``)
+SQUARE_SCHEME_NAMES = ("rank343",)
 
 # pinned digests, as in the reference runtime's generated-module check
 EXPECTED_SHA256 = {
     "rank7": "b374fcc797ea014994453b7502625e24f70ca2f1dcf1bdbe74a716342bfefb1e",
     "rank48": "c7103a1165af22d4e1a417607e9618b0bbae1b69e0c48ed7fa2a5aba26a3bcb7",
     "rank49": "a3c4121dfd09607045255628dd94b60133c24c46b65f1089e89c6564ba522561",
+    "rank343": "c7afccb09f8491e484af1696c25c809757c4af649ee7220e79f25d1c7afe3955",
 }
 
 
@@ -128,6 +131,8 @@ def get_scheme(name: str) -> Scheme:
         scheme = _reduced_scheme("rank49", "rank49-v1", "4x4x4_rank49_159add")
     elif name == "rank48":
         scheme = _slp_scheme("rank48", "rank48-accurate-v1", "4x4x4_rank48_accurate")
+    elif name == "rank343":
+        scheme = _reduced_scheme("rank343", "rank343-mfma-v1", "8x8x8_rank343_1661add")
     else:
         raise ValueError(f"unknown scheme {name!r}")
     if scheme.certificate_sha256 != EXPECTED_SHA256[name]:

@@ -20,6 +20,11 @@ def randn_bf16(shape, seed: int, std: float = 1.0) -> torch.Tensor:
     return (torch.randn(shape, generator=g, dtype=torch.float32) * std).to(torch.bfloat16)
 
 
+def randn_fp16(shape, seed: int, std: float = 1.0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g, dtype=torch.float32) * std).to(torch.float16)
+
+
 def make_linear_inputs(M: int, K: int, N: int, seed: int = 0, bias: bool = False,
                        a_std: float = 1.0, w_std: float = 0.02):
     A = randn_bf16((M, K), seed, a_std)

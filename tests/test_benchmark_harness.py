@@ -200,6 +200,7 @@ def test_validate_outputs_on_cpu_tensors():
     ("rank7", "linear", "op", ("dynamic",), torch.bfloat16),
     ("rank48", "linear", "plan", ("dynamic", "prepacked"), torch.bfloat16),
     ("rank49", "mm", "op", ("dynamic", "prepacked", "external"), torch.float16),
+    ("rank343", "mm", "op", ("dynamic", "prepacked"), torch.float16),
 ])
 def test_report_on_b200(algorithm, operator, implementation, modes, dtype):
     shape = (520, 384, 264)

@@ -16,6 +16,7 @@ from rdna3_fastmm.slp import load_and_verify_slp_certificate, load_slp_program
 RANK48 = CERTIFICATE_ROOT / "4x4x4_rank48_accurate" / "certificate.json"
 RANK49 = CERTIFICATE_ROOT / "4x4x4_rank49_159add" / "certificate.json"
 RANK7 = CERTIFICATE_ROOT / "2x2x2_rank7_15add" / "certificate.json"
+RANK343 = CERTIFICATE_ROOT / "8x8x8_rank343_1661add" / "certificate.json"
 
 
 def test_rank48_slp_certificate_is_exact():
@@ -42,6 +43,7 @@ def test_rank48_vendored_slp_matches_upstream(name, sha256):
 @pytest.mark.parametrize("path,sha256", [
     (RANK7, "b374fcc797ea014994453b7502625e24f70ca2f1dcf1bdbe74a716342bfefb1e"),
     (RANK49, "a3c4121dfd09607045255628dd94b60133c24c46b65f1089e89c6564ba522561"),
+    (RANK343, "c7afccb09f8491e484af1696c25c809757c4af649ee7220e79f25d1c7afe3955"),
 ])
 def test_reduced_certificates_match_upstream(path, sha256):
     assert hashlib.sha256(path.read_bytes()).hexdigest() == sha256
@@ -91,6 +93,32 @@ def test_rank_49_certificate_is_exact():
     assert summary.side_additions == (42, 42, 75)
     assert summary.additions == 159
     assert summary.tensor_entries == 64
+
+
+def test_rank_343_certificate_is_exact():
+    summary = verify_reduced_scheme(load_reduced_scheme(RANK343))
+    assert summary.dimensions == (8, 8, 8)
+    assert (summary.rank, summary.additions, summary.side_additions) == (343, 1661, (462, 456, 743))
+    assert summary.naive_additions == 4434
+
+
+def test_rank343_program_reproduces_the_matrix_multiplication_tensor():
+    """Integer check of the generator's rank-343 programs (numpy: 64^3 entries)."""
+    import numpy as np
+
+    scheme = get_scheme("rank343")
+    U = np.array(scheme.left.coefficients(), dtype=np.int64)    # [343, 64]
+    V = np.array(scheme.right.coefficients(), dtype=np.int64)   # [343, 64]
+    W = np.array(scheme.output.coefficients(), dtype=np.int64)  # [64, 343]
+    T = np.einsum("ri,rj,or->ijo", U, V, W)
+    s = 8
+    E = np.zeros_like(T)
+    for row in range(s):
+        for k in range(s):
+            for col in range(s):
+                E[row * s + k, k * s + col, row * s + col] = 1
+    assert np.array_equal(T, E)
+    assert scheme.certificate_sha256.startswith("c7afccb0")
 
 
 def test_rank_7_certificate_is_exact():
