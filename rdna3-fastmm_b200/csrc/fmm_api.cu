@@ -12,11 +12,13 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "fmm_common.cuh"
 #include "transforms.cuh"
 #include "generated/fmm_schemes.cuh"
 #include "leaf_gemm.cuh"
+#include "reconstruct_tc.cuh"
 
 // Scratch of fmm_linear_noalloc: the L, Rt and P planes of one call live in
 // this array instead of caller-provided buffers.  It is part of the module, so
@@ -86,6 +88,8 @@ struct DeviceInfo {
   bool pair128_configured = false;
   bool pair192_configured = false;
   void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch
+  void* rank343_wt = nullptr;       // device address of g_rank343_wt, once uploaded
+  bool reconstruct_tc_configured = false;
 };
 
 constexpr int kMaxDevices = 64;
@@ -137,7 +141,7 @@ struct SchemeTraits<FMM_SCHEME_RANK7> {
   static constexpr int VEC = 8;
   static constexpr int kInThreads = 256, kInBlocks = 1, kInGrid = 64;
   static constexpr int kOutVec = 8, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 64;
-  static constexpr bool kSumOutput = false;
+  static constexpr bool kTensorCoreOutput = false;
   static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
 };
 template <>
@@ -149,7 +153,7 @@ struct SchemeTraits<FMM_SCHEME_RANK48> {
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 16;
-  static constexpr bool kSumOutput = false;
+  static constexpr bool kTensorCoreOutput = false;
   static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
 };
 template <>
@@ -161,23 +165,23 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 64;
-  static constexpr bool kSumOutput = false;
+  static constexpr bool kTensorCoreOutput = false;
   static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
 };
 // Rank 343: 64 inputs and 343 planes per position.  The input side keeps two
 // elements per thread (64 packed inputs plus the circuit fit in registers);
-// the output side is the +-1 coefficient sum with 64 accumulators of two
-// elements; the K x N right transform stages 64 tiles of 16 x 16.
+// the output side is a tensor-core product with the coefficient matrix
+// (reconstruct_tc.cuh); the K x N right transform stages 64 tiles of 16 x 16.
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK343> {
   using Left = gen::Rank343Left;
   using Right = gen::Rank343Right;
-  using Output = gen::Rank343OutputSum;
+  using Output = gen::Rank343OutputCoefficients;
   static constexpr int S = 8;
   static constexpr int VEC = 2;
   static constexpr int kInThreads = 128, kInBlocks = 1, kInGrid = 16;
   static constexpr int kOutVec = 2, kOutThreads = 128, kOutBlocks = 1, kOutGrid = 16;
-  static constexpr bool kSumOutput = true;
+  static constexpr bool kTensorCoreOutput = true;
   static constexpr int kKnTile = 16, kKnVec = 2, kKnThreads = 128;
 };
 
@@ -205,6 +209,10 @@ int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t 
   return FMM_OK;
 }
 
+template <class Coefs, bool kHalf>
+int launch_reconstruct_tc(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
+                          void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream);
+
 template <int SCHEME, bool kHalf>
 int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                        void* C, int64_t ldc, cudaStream_t stream) {
@@ -215,11 +223,8 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
   const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
   const int64_t items = d.bm * ceil_div(d.bn, V);
   const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
-  if constexpr (T::kSumOutput) {
-    reconstruct_sum_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
-        <<<grid, T::kOutThreads, 0, stream>>>(
-            static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
-            static_cast<uint16_t*>(C), M, N, ldc, vec ? 1 : 0);
+  if constexpr (T::kTensorCoreOutput) {
+    return launch_reconstruct_tc<typename T::Output, kHalf>(P, d, M, N, bias, C, ldc, info, stream);
   } else {
     reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
         <<<grid, T::kOutThreads, 0, stream>>>(
@@ -336,6 +341,23 @@ int plane_map(CUtensorMap* map, const void* base, int64_t k, int64_t rows, int64
   return FMM_OK;
 }
 
+// Generic 3-D FP16 tiled map (128-byte swizzle); strides in bytes.
+int tiled_map_3d(CUtensorMap* map, const void* base, const int64_t (&dims)[3],
+                 const int64_t (&strides)[2], const uint32_t (&box)[3]) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (int rc = tensor_map_encoder(&encode)) return rc;
+  cuuint64_t d[3] = {static_cast<cuuint64_t>(dims[0]), static_cast<cuuint64_t>(dims[1]),
+                     static_cast<cuuint64_t>(dims[2])};
+  cuuint64_t st[2] = {static_cast<cuuint64_t>(strides[0]), static_cast<cuuint64_t>(strides[1])};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), d, st, b,
+                      elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return FMM_OK;
+}
+
 using GemmCfg = LeafGemmConfig<256, 4>;
 using PairCfg256 = LeafGemmPairConfig<256, 6>;
 using PairCfg192 = LeafGemmPairConfig<192, 7>;
@@ -418,6 +440,74 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg>, map_l, map_r, prm);
   if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM (pair) launch");
+  return FMM_OK;
+}
+
+// ------------------------------------------------------------------ rank-343 output
+// W^T of the rank-343 scheme as FP16 [64 outputs][384 products] (+-1 / 0,
+// zero past product 343): one copy per device in static device memory,
+// uploaded on the first rank-343 reconstruct on that device.
+static __device__ __align__(1024) uint16_t g_rank343_wt[kRcN * kRcKPadded];
+
+using RcCfg = ReconstructTcConfig<6>;
+
+template <class Coefs>
+int upload_coefficients(DeviceInfo* info) {
+  static_assert(Coefs::kOutputs == kRcN && Coefs::kInputs == kRcRank, "rank-343 coefficient table");
+  std::lock_guard<std::mutex> lock(g_device_mutex);
+  if (info->rank343_wt != nullptr) return FMM_OK;
+  std::vector<uint16_t> host(size_t(kRcN) * kRcKPadded, 0);
+  for (int o = 0; o < kRcN; ++o)
+    for (int r = 0; r < kRcRank; ++r)
+      host[size_t(o) * kRcKPadded + r] =
+          Coefs::kW[o][r] > 0 ? uint16_t(0x3C00) : (Coefs::kW[o][r] < 0 ? uint16_t(0xBC00) : uint16_t(0));
+  cudaError_t e = cudaMemcpyToSymbol(g_rank343_wt, host.data(), host.size() * sizeof(uint16_t));
+  if (e != cudaSuccess) return cuda_fail(e, "upload of the rank-343 coefficients");
+  void* addr = nullptr;
+  e = cudaGetSymbolAddress(&addr, g_rank343_wt);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_rank343_wt)");
+  info->rank343_wt = addr;
+  return FMM_OK;
+}
+
+template <class Coefs, bool kHalf>
+int launch_reconstruct_tc(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
+                          void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream) {
+  if (int rc = upload_coefficients<Coefs>(info)) return rc;
+  CUtensorMap map_p, map_w;
+  // P[343][bm][ldp] as (position, row, product); box 64 positions x 1 row x 64 products
+  if (int rc = tiled_map_3d(&map_p, P, {d.ldp, d.bm, kRcRank}, {d.ldp * 2, d.bm * d.ldp * 2},
+                            {64u, 1u, static_cast<uint32_t>(kRcK)}))
+    return rc;
+  if (int rc = tiled_map_3d(&map_w, info->rank343_wt, {kRcKPadded, kRcN, 1},
+                            {int64_t(kRcKPadded) * 2, int64_t(kRcKPadded) * kRcN * 2},
+                            {static_cast<uint32_t>(kRcK), static_cast<uint32_t>(kRcN), 1u}))
+    return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (int rc = ensure_smem_attribute(info->reconstruct_tc_configured,
+                                       reconstruct_tc_kernel<RcCfg, kHalf>, RcCfg::kSmemBytes))
+      return rc;
+  }
+  ReconstructTcParams prm;
+  prm.bm = d.bm;
+  prm.bn = d.bn;
+  prm.M = M;
+  prm.N = N;
+  prm.ldc = ldc;
+  const int64_t per_row = ceil_div(d.bn, kRcM);
+  if (d.bm * per_row > 0x7fffffff) return fail(FMM_ERR_TOO_LARGE, "too many reconstruct tiles");
+  prm.tiles_per_row = static_cast<int32_t>(per_row);
+  prm.total_tiles = static_cast<int32_t>(d.bm * per_row);
+  prm.vector_stores = (d.bn % 8 == 0 && ldc % 8 == 0 && aligned(C, 16)) ? 1 : 0;
+  prm.bias = static_cast<const uint16_t*>(bias);
+  prm.C = static_cast<uint16_t*>(C);
+  prm.timeout_ns = g_timeout_ns;
+  const int sms = usable_sms(info);
+  const int grid = prm.total_tiles < sms ? prm.total_tiles : sms;
+  reconstruct_tc_kernel<RcCfg, kHalf><<<grid, kRcThreads, RcCfg::kSmemBytes, stream>>>(map_p, map_w, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "rank-343 reconstruct launch");
   return FMM_OK;
 }
 

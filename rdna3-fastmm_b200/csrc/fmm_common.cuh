@@ -244,10 +244,26 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t addr) {
          ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
 
+// Shared-memory descriptor for an MN-major operand with 128-byte swizzling:
+// atoms of 64 FP16 along M/N (one 128-byte row) x 8 rows along K, 1024 bytes;
+// `lbo_bytes` steps between atoms along M/N, `sbo_bytes` between 8-row groups
+// along K (the canonical MN-major SWIZZLE_128B layout of the UMMA
+// descriptor).  Atoms must start on 1024-byte boundaries.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t addr, uint32_t lbo_bytes,
+                                                       uint32_t sbo_bytes) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
 // Instruction descriptor, kind::f16: FP16 A and B (both K-major), FP32 D,
 // M = 128, N = n.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {
   return (1u << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Same with A MN-major (bit 15: "transpose A"); B stays K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32_a_mn(uint32_t m, uint32_t n) {
+  return idesc_f16_f32(m, n) | (1u << 15);
 }
 
 }  // namespace fmm

@@ -291,41 +291,6 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
   }
 }
 
-// Output side as a +-1 coefficient sum (``Prog::accumulate``), for schemes
-// whose product count is too large to keep every product of a position in
-// registers (rank 343): each thread owns VEC consecutive plane columns and
-// Prog::kOutputs FP32 accumulators starting at +0; the generated code reads
-// the products a group at a time, in ascending order, and adds or subtracts
-// each into the outputs it feeds.
-template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = true>
-__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_sum_kernel(
-    const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
-    const uint16_t* __restrict__ bias, uint16_t* __restrict__ C, int64_t M, int64_t N,
-    int64_t ldc, int vector_stores) {
-  using Raw = typename VecIO<VEC>::H;
-  const int64_t plane = bm * ldp;
-  const uint32_t vecs_per_row = static_cast<uint32_t>((bn + VEC - 1) / VEC);
-  const uint32_t total = static_cast<uint32_t>(bm) * vecs_per_row;
-  for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += gridDim.x * blockDim.x) {
-    const uint32_t i = idx / vecs_per_row;
-    const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
-    const __half* base = P + static_cast<int64_t>(i) * ldp + j;
-    VecF<VEC> acc[Prog::kOutputs];
-#pragma unroll
-    for (int o = 0; o < Prog::kOutputs; ++o)
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) acc[o].v[e] = 0.0f;
-    auto in = [&](int r) -> VecF<VEC> {
-      return unpack_half<VEC>(__ldg(reinterpret_cast<const Raw*>(base + r * plane)));
-    };
-    Prog::template accumulate<VecF<VEC>>(in, acc);
-#pragma unroll
-    for (int o = 0; o < Prog::kOutputs; ++o)
-      store_output_vector<S, VEC, kHalfOut>(o, acc[o], i, j, bm, bn, bias, C, M, N, ldc, vector_stores);
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Right transform of a contiguous B[K, N] (the plain-mm API): the program's
 // input q is block (q / S, q % S) of B and the planes come out K-major,
