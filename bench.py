@@ -195,8 +195,13 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         if M_total % (world * args.chunks):
             raise SystemExit("--shard needs M divisible by gpus * chunks")
         M = M_total // world
-        description += (f"; rows sharded block-cyclically over {world} GPUs in {args.chunks} chunks, "
-                        f"output all-gathered (NCCL) chunk by chunk, overlapped with compute")
+        if args.transport == "p2p":
+            description += (f"; rows sharded block-cyclically over {world} GPUs in {args.chunks} chunks, "
+                            f"output gathered by the reconstruct kernel itself (stores into every "
+                            f"rank's symmetric buffer over NVLink), overlapped with compute")
+        else:
+            description += (f"; rows sharded block-cyclically over {world} GPUs in {args.chunks} chunks, "
+                            f"output all-gathered (NCCL) chunk by chunk, overlapped with compute")
     else:
         M = M_total
     plan = plans[scheme](M, K, N, device, dtype=torch.bfloat16, compute_dtype=torch.float16)
@@ -258,9 +263,11 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     if shard:
         from rdna3_fastmm.distributed import RowShardedLinear
 
+        p2p = args.transport == "p2p"
         layer = RowShardedLinear(plans[scheme], M_total, W, bias=bias, chunks=args.chunks,
-                                 reserve_sms=args.reserve_sms, max_free_memory_fraction=0.9)
-        gathered = layer.gather_buffer()
+                                 reserve_sms=args.reserve_sms,
+                                 max_free_memory_fraction=0.9, transport=args.transport)
+        gathered = None if p2p else layer.gather_buffer()
         for _ in range(args.warmup):
             flush.zero_()
             layer(A, out=gathered)
@@ -321,7 +328,8 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     b_d = torch.empty_like(bias) if bias is not None else None
 
     if shard:
-        C_pin = torch.empty(tuple(gathered.shape), dtype=torch.bfloat16).pin_memory()
+        C_pin = torch.empty((layer.rows if gathered is None else gathered.shape[0], N),
+                            dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
         A_d.copy_(A_pin, non_blocking=True)
@@ -410,7 +418,9 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         "config": {"workload": f"{args.workload}: {description}", "scheme": scheme,
                    "M": M, "K": K, "N": N, "bias": with_bias, "prepacked": prepacked,
                    "l2": "flushed (256 MiB write) before every step",
-                   "parallelism": (f"rows sharded x{world} + NCCL all-gather" if shard else
+                   "parallelism": (f"rows sharded x{world} + "
+                                   + ("fused reconstruct/all-gather over NVLink peer memory"
+                                      if args.transport == "p2p" else "NCCL all-gather") if shard else
                                    f"replicas x{world}" if world > 1 else "single GPU")},
         "roofline": {"bound": "tensor", "kernel": "leaf_gemm", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 3),
@@ -460,7 +470,11 @@ def main() -> None:
     parser.add_argument("--chunks", type=int, default=4,
                         help="row chunks per rank in --shard mode (gather overlaps compute)")
     parser.add_argument("--reserve-sms", type=int, default=32,
-                        help="SMs left free for NCCL while --shard chunks compute")
+                        help="SMs the GEMM leaves free, while --shard chunks compute, for the NCCL "
+                             "all-gather or the gathering reconstruct of the previous chunk")
+    parser.add_argument("--transport", choices=("nccl", "p2p"), default="nccl",
+                        help="--shard gather: NCCL all-gather, or the reconstruct kernel storing "
+                             "into every rank's symmetric buffer over NVLink")
     parser.add_argument("--profile", action="store_true",
                         help="timed steps only: no cuBLAS, e2e, parity or CPU legs")
     args = parser.parse_args()

@@ -117,6 +117,21 @@ int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t b
 int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, const void* bias,
                     void* C, int64_t ldc, fmm_stream_t stream);
 
+/* Row-sharded linear, output transform fused with the all-gather: like
+ * fmm_reconstruct, but every output element is stored into all `ndest`
+ * destinations (1..8) at once -- this rank's own gather buffer and the
+ * peers' buffers mapped into this process (CUDA peer / symmetric-memory
+ * pointers reached over NVLink), each pointing at this rank's first row of
+ * the gathered [rows, N] output, with leading dimension `ldc`.  The stores
+ * end with a system-scope fence; the caller signals peers (a barrier on the
+ * same stream) before they read.  Circuit schemes only (7, 48, 49); rank 343
+ * returns FMM_ERR_UNSUPPORTED.  No reference counterpart: the reference is
+ * single-GPU; this replaces the reconstruct + NCCL all-gather pair of the
+ * multi-GPU form (rdna3_fastmm/distributed.py). */
+int fmm_reconstruct_gather(int scheme, int dtype, const void* P, int64_t M, int64_t N,
+                           const void* bias, void* const* dests, int ndest, int64_t ldc,
+                           fmm_stream_t stream);
+
 /* The whole product through the scheme, using the caller's planes (L, Rt, P
  * sized by fmm_plan_dims): C = A * weight^T (+ bias) for F.linear, or, with
  * FMM_RIGHT_KN, C = A * B for a contiguous B[K,N].  With FMM_LINEAR_PREPACKED,

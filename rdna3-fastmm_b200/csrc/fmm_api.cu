@@ -237,6 +237,31 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
 }
 
 template <int SCHEME, bool kHalf>
+int launch_reconstruct_gather(const void* P, const fmm_dims& d, int64_t M, int64_t N,
+                              const void* bias, const GatherDests& dests, int64_t ldc,
+                              cudaStream_t stream) {
+  using T = SchemeTraits<SCHEME>;
+  if constexpr (T::kTensorCoreOutput) {
+    return fail(FMM_ERR_UNSUPPORTED, "the gathering reconstruct covers the circuit schemes (7, 48, 49)");
+  } else {
+    constexpr int V = T::kOutVec;
+    DeviceInfo* info = nullptr;
+    if (int rc = device_info(&info)) return rc;
+    bool vec = (d.bn % V == 0) && (ldc % V == 0);
+    for (int k = 0; k < dests.n; ++k) vec = vec && aligned(dests.p[k], 2 * V);
+    const int64_t items = d.bm * ceil_div(d.bn, V);
+    const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
+    reconstruct_gather_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
+        <<<grid, T::kOutThreads, 0, stream>>>(static_cast<const __half*>(P), d.bm, d.bn, d.ldp,
+                                              static_cast<const uint16_t*>(bias), dests, M, N, ldc,
+                                              vec ? 1 : 0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "gathering reconstruct launch");
+    return FMM_OK;
+  }
+}
+
+template <int SCHEME, bool kHalf>
 int launch_right_kn(const void* B, int64_t K, int64_t N, int64_t ldb, void* dst, const fmm_dims& d,
                     cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
@@ -287,6 +312,13 @@ struct RightKnOp {
   static int run(const void* B, int64_t K, int64_t N, int64_t ldb, void* Rt, const fmm_dims* d,
                  cudaStream_t s) {
     return launch_right_kn<SC, H>(B, K, N, ldb, Rt, *d, s);
+  }
+};
+template <int SC, bool H>
+struct ReconstructGatherOp {
+  static int run(const void* P, const fmm_dims* d, int64_t M, int64_t N, const void* bias,
+                 const GatherDests* dests, int64_t ldc, cudaStream_t s) {
+    return launch_reconstruct_gather<SC, H>(P, *d, M, N, bias, *dests, ldc, s);
   }
 };
 template <int SC, bool H>
@@ -657,6 +689,27 @@ int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, 
   if (!aligned(P, 16)) return fail(FMM_ERR_MISALIGNED, "P must be 16-byte aligned");
   return dispatch<ReconstructOp>(scheme, dtype, P, &d, M, N, bias, C, ldc,
                                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fmm_reconstruct_gather(int scheme, int dtype, const void* P, int64_t M, int64_t N,
+                           const void* bias, void* const* dests, int ndest, int64_t ldc,
+                           fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, M, 1, N, &d)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (P == nullptr || dests == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  if (ndest < 1 || ndest > kMaxGatherDests)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "ndest must be in [1, 8]");
+  if (ldc < N) return fail(FMM_ERR_INVALID_ARGUMENT, "ldc < N");
+  if (!aligned(P, 16)) return fail(FMM_ERR_MISALIGNED, "P must be 16-byte aligned");
+  GatherDests list = {};
+  list.n = ndest;
+  for (int k = 0; k < ndest; ++k) {
+    if (dests[k] == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null destination");
+    list.p[k] = static_cast<uint16_t*>(dests[k]);
+  }
+  return dispatch<ReconstructGatherOp>(scheme, dtype, P, &d, M, N, bias, &list, ldc,
+                                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fmm_linear(int scheme, int dtype, const void* A, const void* W, const void* bias, void* C,

@@ -292,6 +292,78 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Reconstruct fused with the all-gather of a row-sharded linear: every output
+// vector is stored into `n` copies of the gathered output at once -- this
+// rank's own buffer and its peers' buffers mapped into this process (NVLink
+// peer memory), each pointer already offset to this rank's first row.  The
+// arithmetic and rounding are reconstruct_kernel's; only the store fans out,
+// so the transfer over NVLink overlaps the recombination vector by vector and
+// no separate collective runs.  A system-scope fence at the end orders the
+// peer stores before whatever the caller uses to signal completion.
+constexpr int kMaxGatherDests = 8;
+struct GatherDests {
+  uint16_t* p[kMaxGatherDests];
+  int n;
+};
+
+template <int S, int VEC, bool kHalfOut>
+__device__ __forceinline__ void store_output_vector_all(int o, const VecF<VEC>& x, int64_t i, int64_t j,
+                                                        int64_t bm, int64_t bn,
+                                                        const uint16_t* __restrict__ bias,
+                                                        const GatherDests& dests, int64_t M, int64_t N,
+                                                        int64_t ldc, int vector_stores) {
+  const int br = o / S, bc = o % S;
+  const int64_t row = br * bm + i;
+  if (row >= M) return;
+  const int64_t c0 = bc * bn + j;
+  VecF<VEC> y = x;
+  if (bias != nullptr) {
+    VecF<VEC> b;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e)
+      b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
+    y = vadd(x, b);
+  }
+  const int64_t offset = row * ldc + c0;
+  if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
+    for (int d = 0; d < dests.n; ++d) store_out_vec<kHalfOut, VEC>(dests.p[d] + offset, y);
+  } else {
+    for (int d = 0; d < dests.n; ++d) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e)
+        if (j + e < bn && c0 + e < N) dests.p[d][offset + e] = round_out<kHalfOut>(y.v[e]);
+    }
+  }
+}
+
+template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_gather_kernel(
+    const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
+    const uint16_t* __restrict__ bias, const GatherDests dests, int64_t M, int64_t N, int64_t ldc,
+    int vector_stores) {
+  using Raw = typename VecIO<VEC>::H;
+  const int64_t plane = bm * ldp;
+  const uint32_t vecs_per_row = static_cast<uint32_t>((bn + VEC - 1) / VEC);
+  const uint32_t total = static_cast<uint32_t>(bm) * vecs_per_row;
+  for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += gridDim.x * blockDim.x) {
+    const uint32_t i = idx / vecs_per_row;
+    const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
+    Raw raw[Prog::kInputs];
+#pragma unroll
+    for (int r = 0; r < Prog::kInputs; ++r)
+      raw[r] = __ldg(reinterpret_cast<const Raw*>(P + r * plane + static_cast<int64_t>(i) * ldp + j));
+    auto in = [&](int r) -> VecF<VEC> { return unpack_half<VEC>(raw[r]); };
+    auto out = [&](int o, const VecF<VEC>& x) {
+      store_output_vector_all<S, VEC, kHalfOut>(o, x, i, j, bm, bn, bias, dests, M, N, ldc,
+                                                vector_stores);
+    };
+    Prog::template run<VecF<VEC>>(in, out);
+  }
+  __threadfence_system();
+}
+
+// ---------------------------------------------------------------------------
 // Right transform of a contiguous B[K, N] (the plain-mm API): the program's
 // input q is block (q / S, q % S) of B and the planes come out K-major,
 // Rt[r][n][k], so each block is transposed on the way.  A CTA owns one

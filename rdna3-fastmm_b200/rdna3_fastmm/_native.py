@@ -59,6 +59,11 @@ _SIGNATURES = {
     "fmm_transform_b": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_leaf_gemm": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_reconstruct": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _P, _P, _I64, _P], ctypes.c_int),
+    "fmm_reconstruct_gather": (
+        [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _P, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+         _I64, _P],
+        ctypes.c_int,
+    ),
     "fmm_linear": (
         [ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P, _P, ctypes.c_uint, _P],
         ctypes.c_int,
@@ -158,6 +163,16 @@ def leaf_gemm(rank: int, L, Rt, bm: int, bn: int, bk: int, P) -> None:
 def reconstruct(scheme: str, P, M: int, N: int, bias, C) -> None:
     check(library().fmm_reconstruct(SCHEME_IDS[scheme], dtype_id(C.dtype), _ptr(P), M, N, _ptr(bias),
                                     _ptr(C), C.stride(0), _stream(P.device)), "fmm_reconstruct")
+
+
+def reconstruct_gather(scheme: str, P, M: int, N: int, bias, dests: list[int], ldc: int, dtype) -> None:
+    """Output transform storing this rank's rows into every buffer in
+    ``dests`` (device addresses of this rank's first row in the own and the
+    peers' gathered outputs, leading dimension ``ldc``)."""
+    array = (ctypes.c_void_p * len(dests))(*dests)
+    check(library().fmm_reconstruct_gather(SCHEME_IDS[scheme], dtype_id(dtype), _ptr(P), M, N, _ptr(bias),
+                                           array, len(dests), ldc, _stream(P.device)),
+          "fmm_reconstruct_gather")
 
 
 def linear(scheme: str, A, W, bias, C, L, Rt, P, prepacked: bool, right_kn: bool = False) -> None:

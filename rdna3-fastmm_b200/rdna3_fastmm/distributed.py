@@ -15,6 +15,17 @@ chunk is computed on the current stream and its slice is all-gathered
 asynchronously while the next chunk computes, overlapping NVLink traffic with
 tensor-core work.
 
+``transport="p2p"`` replaces the reconstruct + NCCL all-gather pair by one
+kernel (``fmm_reconstruct_gather``): the gather buffer is symmetric memory
+(``torch.distributed._symmetric_memory``), and each rank's output transform
+stores every output vector into its own buffer and, over NVLink, into every
+peer's buffer at this rank's rows.  With ``chunks > 1`` the gathering
+reconstruct of chunk c runs on a side stream while chunk c + 1 transforms and
+multiplies (two product workspaces alternate), so NVLink traffic overlaps
+tensor-core work without reserving SMs for a collective.  A one-element
+all-reduce queued behind the kernels makes every peer's rows visible before
+the result is used.
+
 The reference is single-GPU; this is the multi-GPU form north_star asks for
 (M sharded across 1/2/4/8 GPUs, weight replicated, all-gather on demand).
 """
@@ -56,7 +67,12 @@ class RowShardedLinear:
     def __init__(self, plan_type, rows: int, weight: torch.Tensor, *, group=None,
                  bias: Optional[torch.Tensor] = None, chunks: int = 1, reserve_sms: int = 0,
                  local_linear: Optional[Callable[[torch.Tensor, torch.Tensor], None]] = None,
-                 max_free_memory_fraction: float = 0.75) -> None:
+                 max_free_memory_fraction: float = 0.75, transport: str = "nccl") -> None:
+        if transport not in ("nccl", "p2p"):
+            raise ValueError("transport must be 'nccl' or 'p2p'")
+        if transport == "p2p" and local_linear is not None:
+            raise ValueError("the p2p transport runs the B200 plan, not a local stand-in")
+        self.transport = transport
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -89,6 +105,70 @@ class RowShardedLinear:
             self.packed = self.plan.pack_weight(weight, max_free_memory_fraction)
             self.workspace = self.plan.allocate_workspace(max_free_memory_fraction, prepacked_right=True)
             self._local = self._plan_linear
+        if transport == "p2p":
+            self._setup_p2p(max_free_memory_fraction)
+
+    def _setup_p2p(self, max_free_memory_fraction: float) -> None:
+        import torch.distributed._symmetric_memory as symm
+
+        if self.world > 8:
+            raise ValueError("the gathering reconstruct stores to at most 8 ranks")
+        if self.bias is not None and self.bias.dtype != torch.bfloat16:
+            raise ValueError("bias must be BF16")
+        # exact [M, N] rows: every rank writes its own rows, no padding slots
+        self._symm_out = symm.empty(self.rows, self.columns, dtype=torch.bfloat16, device=self.device)
+        group = self.group if self.group is not None else dist.group.WORLD
+        self._symm = symm.rendezvous(self._symm_out, group)
+        self._peer_bases = [int(p) for p in self._symm.buffer_ptrs]
+        # a second product workspace so chunk c's gathering reconstruct can
+        # read its products while chunk c + 1 multiplies
+        self._products = [self.workspace.products]
+        if self.chunks > 1:
+            self._products.append(torch.empty_like(self.workspace.products))
+        self._side = torch.cuda.Stream(device=self.device)
+        self._flag = torch.zeros(1, device=self.device, dtype=torch.int32)
+
+    def _p2p(self, local_rows: torch.Tensor) -> torch.Tensor:
+        main = torch.cuda.current_stream(self.device)
+        row_bytes = self.columns * 2
+        done: list = [None] * len(self._products)
+        # with chunks the GEMM of chunk c + 1 leaves `reserve_sms` SMs to the
+        # gathering reconstruct of chunk c, which runs beside it
+        budget = self._reserve() if self.chunks > 1 else False
+        try:
+            self._p2p_chunks(local_rows, main, row_bytes, done)
+        finally:
+            self._release(budget)
+        main.wait_stream(self._side)
+        # completion: an all-reduce queued behind the gathering kernels ends on
+        # a rank only after every rank's kernels (and their fenced peer
+        # stores) have finished; NCCL's process-group timeout bounds the wait
+        dist.all_reduce(self._flag, group=self.group)
+        return self._symm_out
+
+    def _p2p_chunks(self, local_rows: torch.Tensor, main, row_bytes: int, done: list) -> None:
+        from . import _native
+
+        plan, ws = self.plan, self.workspace
+        s = plan.shape
+        for c, (start, count) in enumerate(self.row_blocks()):
+            k = c % len(self._products)
+            P = self._products[k]
+            if done[k] is not None:
+                main.wait_event(done[k])  # the side stream has finished reading P
+            _native.transform_a(plan.scheme, local_rows[c * self.chunk_rows:c * self.chunk_rows + count],
+                                ws.left_transformed)
+            _native.leaf_gemm(plan.rank, ws.left_transformed, self.packed.transformed, s.block_rows,
+                              s.block_columns, s.block_inner, P)
+            ready = torch.cuda.Event()
+            ready.record(main)
+            self._side.wait_event(ready)
+            with torch.cuda.stream(self._side):
+                dests = [base + start * row_bytes for base in self._peer_bases]
+                _native.reconstruct_gather(plan.scheme, P, count, self.columns, self.bias, dests,
+                                           self.columns, torch.bfloat16)
+            done[k] = torch.cuda.Event()
+            done[k].record(self._side)
 
     def _plan_linear(self, local_rows: torch.Tensor, out: torch.Tensor) -> None:
         self.plan.run_linear_packed(local_rows, self.packed, self.workspace, self.bias, out)
@@ -127,11 +207,17 @@ class RowShardedLinear:
     def __call__(self, local_rows: torch.Tensor, *, gather: bool = True,
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Run this rank's rows; with ``gather`` return the whole ``C[M, N]``
-        on every rank, else this rank's ``[count, N]`` rows (local order)."""
+        on every rank, else this rank's ``[count, N]`` rows (local order).
+        With the p2p transport the gathered result is the layer's symmetric
+        buffer, overwritten by the next call."""
         if tuple(local_rows.shape) != (self.count, self.inner):
             raise ValueError(f"local rows have shape {tuple(local_rows.shape)}, "
                              f"expected {(self.count, self.inner)}")
         ch = self.chunk_rows
+        if gather and self.transport == "p2p":
+            if out is not None:
+                raise ValueError("the p2p transport gathers into its own symmetric buffer")
+            return self._p2p(local_rows)
         if not gather:
             result = out if out is not None else torch.empty(
                 (self.count, self.columns), device=self.device, dtype=torch.bfloat16)
