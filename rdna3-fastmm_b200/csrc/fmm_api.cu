@@ -180,7 +180,6 @@ struct SchemeTraits<FMM_SCHEME_RANK343> {
   static constexpr int S = 8;
   static constexpr int VEC = 2;
   static constexpr int kInThreads = 128, kInBlocks = 1, kInGrid = 16;
-  static constexpr int kOutVec = 2, kOutThreads = 128, kOutBlocks = 1, kOutGrid = 16;
   static constexpr bool kTensorCoreOutput = true;
   static constexpr int kKnTile = 16, kKnVec = 2, kKnThreads = 128;
 };
@@ -217,23 +216,23 @@ template <int SCHEME, bool kHalf>
 int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                        void* C, int64_t ldc, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
-  constexpr int V = T::kOutVec;
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
-  const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
-  const int64_t items = d.bm * ceil_div(d.bn, V);
-  const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
   if constexpr (T::kTensorCoreOutput) {
     return launch_reconstruct_tc<typename T::Output, kHalf>(P, d, M, N, bias, C, ldc, info, stream);
   } else {
+    constexpr int V = T::kOutVec;
+    const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
+    const int64_t items = d.bm * ceil_div(d.bn, V);
+    const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
     reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
         <<<grid, T::kOutThreads, 0, stream>>>(
             static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
             static_cast<uint16_t*>(C), M, N, ldc, vec ? 1 : 0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
+    return FMM_OK;
   }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
-  return FMM_OK;
 }
 
 template <int SCHEME, bool kHalf>

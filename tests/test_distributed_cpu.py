@@ -91,3 +91,22 @@ def test_failed_rank_becomes_an_error_not_a_hang():
     results = _run(2, 64, "fail")
     assert results[1] == "left"
     assert str(results[0]).startswith("error")
+
+
+def test_transport_arguments_are_validated():
+    store = dist.HashStore()
+    dist.init_process_group("gloo", store=store, rank=0, world_size=1)
+    try:
+        W = torch.zeros((8, 4), dtype=torch.bfloat16)
+
+        def local(x, out):
+            out.copy_(torch.nn.functional.linear(x, W))
+
+        with pytest.raises(ValueError, match="transport"):
+            RowShardedLinear(None, 16, W, local_linear=local, transport="nvshmem")
+        with pytest.raises(ValueError, match="p2p transport runs the B200 plan"):
+            RowShardedLinear(None, 16, W, local_linear=local, transport="p2p")
+        layer = RowShardedLinear(None, 16, W, local_linear=local, transport="nccl")
+        assert layer.transport == "nccl"
+    finally:
+        dist.destroy_process_group()
