@@ -223,12 +223,13 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
   } else {
     constexpr int V = T::kOutVec;
     const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
+    const bool vec_bias = (d.bn % V == 0) && bias != nullptr && aligned(bias, 2 * V);
     const int64_t items = d.bm * ceil_div(d.bn, V);
     const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
     reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
         <<<grid, T::kOutThreads, 0, stream>>>(
             static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
-            static_cast<uint16_t*>(C), M, N, ldc, vec ? 1 : 0);
+            static_cast<uint16_t*>(C), M, N, ldc, (vec ? 1 : 0) | (vec_bias ? 2 : 0));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
     return FMM_OK;
@@ -248,12 +249,13 @@ int launch_reconstruct_gather(const void* P, const fmm_dims& d, int64_t M, int64
     if (int rc = device_info(&info)) return rc;
     bool vec = (d.bn % V == 0) && (ldc % V == 0);
     for (int k = 0; k < dests.n; ++k) vec = vec && aligned(dests.p[k], 2 * V);
+    const bool vec_bias = (d.bn % V == 0) && bias != nullptr && aligned(bias, 2 * V);
     const int64_t items = d.bm * ceil_div(d.bn, V);
     const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
     reconstruct_gather_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
         <<<grid, T::kOutThreads, 0, stream>>>(static_cast<const __half*>(P), d.bm, d.bn, d.ldp,
                                               static_cast<const uint16_t*>(bias), dests, M, N, ldc,
-                                              vec ? 1 : 0);
+                                              (vec ? 1 : 0) | (vec_bias ? 2 : 0));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "gathering reconstruct launch");
     return FMM_OK;

@@ -225,8 +225,26 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
 // recombination, then rounded to nearest even (BF16 or FP16).  `raw` holds the
 // R product vectors, already loaded.  Shared by the reconstruct kernel and the
 // fused rank-7 epilogue of the leaf GEMM, so both round identically.
+// Bias of one output vector, widened to FP32: one vector load when the
+// vector is interior and the bias aligned (bit 1 of `vector_flags`), else
+// element loads with zeros past the edges.
+template <int VEC, bool kHalfOut>
+__device__ __forceinline__ VecF<VEC> load_bias_vector(const uint16_t* __restrict__ bias, int64_t j,
+                                                      int64_t c0, int64_t bn, int64_t N,
+                                                      int vector_flags) {
+  if ((vector_flags & 2) && j + VEC <= bn && c0 + VEC <= N)
+    return unpack_in<kHalfOut, VEC>(__ldg(reinterpret_cast<const typename VecIO<VEC>::BF*>(bias + c0)));
+  VecF<VEC> b;
+#pragma unroll
+  for (int e = 0; e < VEC; ++e)
+    b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
+  return b;
+}
+
 // Store output o (C block (o / S, o % S)) of one vector position: optional
 // bias, then one rounding to the output format; ragged edges element-wise.
+// `vector_stores`: bit 0 = C rows allow vector stores, bit 1 = bias allows
+// vector loads.
 template <int S, int VEC, bool kHalfOut>
 __device__ __forceinline__ void store_output_vector(int o, const VecF<VEC>& x, int64_t i, int64_t j,
                                                     int64_t bm, int64_t bn,
@@ -238,15 +256,9 @@ __device__ __forceinline__ void store_output_vector(int o, const VecF<VEC>& x, i
   if (row >= M) return;
   const int64_t c0 = bc * bn + j;
   VecF<VEC> y = x;
-  if (bias != nullptr) {
-    VecF<VEC> b;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e)
-      b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
-    y = vadd(x, b);
-  }
+  if (bias != nullptr) y = vadd(x, load_bias_vector<VEC, kHalfOut>(bias, j, c0, bn, N, vector_stores));
   uint16_t* dst = C + row * ldc + c0;
-  if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
+  if ((vector_stores & 1) && j + VEC <= bn && c0 + VEC <= N) {
     store_out_vec<kHalfOut, VEC>(dst, y);
   } else {
 #pragma unroll
@@ -317,15 +329,9 @@ __device__ __forceinline__ void store_output_vector_all(int o, const VecF<VEC>& 
   if (row >= M) return;
   const int64_t c0 = bc * bn + j;
   VecF<VEC> y = x;
-  if (bias != nullptr) {
-    VecF<VEC> b;
-#pragma unroll
-    for (int e = 0; e < VEC; ++e)
-      b.v[e] = (j + e < bn && c0 + e < N) ? widen_in<kHalfOut>(bias[c0 + e]) : 0.0f;
-    y = vadd(x, b);
-  }
+  if (bias != nullptr) y = vadd(x, load_bias_vector<VEC, kHalfOut>(bias, j, c0, bn, N, vector_stores));
   const int64_t offset = row * ldc + c0;
-  if (vector_stores && j + VEC <= bn && c0 + VEC <= N) {
+  if ((vector_stores & 1) && j + VEC <= bn && c0 + VEC <= N) {
     for (int d = 0; d < dests.n; ++d) store_out_vec<kHalfOut, VEC>(dests.p[d] + offset, y);
   } else {
     for (int d = 0; d < dests.n; ++d) {

@@ -146,6 +146,10 @@ def test_fx_rewrite_leaves_unmeasured_shapes_on_cublas():
 
 
 def test_compiled_model_runs_through_the_backend():
+    # in-tree use: importing the backend module registers "rdna3-fastmm"
+    # (an installed package registers it through its entry point)
+    import rdna3_fastmm.inductor  # noqa: F401
+
     model = _FunctionalModel(64, 96, 32).to(DEVICE)
     x = torch.randn((4, 64), device=DEVICE, dtype=torch.bfloat16)
     with torch.no_grad():

@@ -88,6 +88,28 @@ def test_reconstruct_matches_oracle_bitwise(name, shape, with_bias):
     np.testing.assert_array_equal(_bits(C), oracle.bf16_bits(ref).view(np.int16))
 
 
+@pytest.mark.parametrize("name", list(PLANS))
+def test_reconstruct_unaligned_bias_matches_aligned(name):
+    """Bias vector loads (aligned bias) and element loads (offset bias) add the
+    same values: identical bits."""
+    M, K, N = 130, 64, 2064
+    _, _, bias = make_linear_inputs(M, K, N, seed=0, bias=True)
+    s, _, _, P = _planes(PLANS[name], M, K, N)
+    products = random_products(PLANS[name].rank, s.block_rows, s.block_columns, seed=4)
+    P.zero_()
+    P[:, :, : s.block_columns] = products.cuda()
+    store = torch.empty(N + 1, device="cuda", dtype=torch.bfloat16)
+    store[1:] = bias.cuda()
+    C1 = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    C2 = torch.empty_like(C1)
+    _native.reconstruct(name, P, M, N, bias.cuda(), C1)
+    _native.reconstruct(name, P, M, N, store[1:], C2)
+    torch.cuda.synchronize()
+    assert torch.equal(C1.view(torch.int16), C2.view(torch.int16))
+    ref = oracle.output_transform(name, products.numpy(), M, N, f32(bias))
+    np.testing.assert_array_equal(_bits(C1), oracle.bf16_bits(ref).view(np.int16))
+
+
 @pytest.mark.parametrize("variant", ["single", "pair256", "pair128"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
