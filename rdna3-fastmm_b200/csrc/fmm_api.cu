@@ -392,7 +392,7 @@ int tiled_map_3d(CUtensorMap* map, const void* base, const int64_t (&dims)[3],
 }
 
 using GemmCfg = LeafGemmConfig<256, 4>;
-using PairCfg256 = LeafGemmPairConfig<256, 6>;
+using PairCfg256 = LeafGemmPairConfig<256, 7>;
 using PairCfg192 = LeafGemmPairConfig<192, 7>;
 using PairCfg128 = LeafGemmPairConfig<128, 8>;
 
@@ -400,9 +400,9 @@ enum GemmVariant { kVariantSingle = 0, kVariantPair256 = 1, kVariantPair128 = 2,
 
 // Estimated relative cost of a variant: whole waves of tiles over the SMs (or
 // SM pairs), times the padded work one SM does per tile, divided by the
-// variant's measured tensor-pipe efficiency relative to the 1-SM 128x256 tile
-// (a pair stages half of B per SM; 256x128 pairs are slower than one SM,
-// see DESIGN.md, and are only used when forced).
+// variant's measured throughput relative to the 1-SM 128x256 tile on B200
+// leaf shapes (a pair stages half of B per SM; 256x192 pairs measured 0.90 -
+// 0.97 of one SM, 256x128 pairs slower still and only used when forced).
 double variant_cost(int variant, int64_t rank, int64_t bm, int64_t bn, int sms) {
   const bool pair = variant != kVariantSingle;
   const int64_t tm = pair ? 256 : 128;
@@ -410,7 +410,7 @@ double variant_cost(int variant, int64_t rank, int64_t bm, int64_t bn, int sms) 
   const int64_t units = pair ? sms / 2 : sms;
   const double efficiency = variant == kVariantSingle    ? 1.0
                             : variant == kVariantPair256 ? 1.15
-                            : variant == kVariantPair192 ? 1.08
+                            : variant == kVariantPair192 ? 0.95
                                                          : 0.70;
   const int64_t tiles = rank * ceil_div(bm, tm) * ceil_div(bn, tn);
   const int64_t waves = ceil_div(tiles, units);

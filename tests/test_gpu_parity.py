@@ -110,7 +110,7 @@ def test_reconstruct_unaligned_bias_matches_aligned(name):
     np.testing.assert_array_equal(_bits(C1), oracle.bf16_bits(ref).view(np.int16))
 
 
-@pytest.mark.parametrize("variant", ["single", "pair256", "pair128"])
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair192", "pair128"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
     [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (2, 129, 257, 1000), (48, 64, 72, 130),
