@@ -305,6 +305,7 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     rel = float(torch.linalg.vector_norm(got - exact) / torch.linalg.vector_norm(exact))
     native_rows = torch.nn.functional.linear(A[rows], W, bias).double()
     native_rel = float(torch.linalg.vector_norm(native_rows - exact) / torch.linalg.vector_norm(exact))
+    nonfinite = int((~torch.isfinite(out)).sum())  # over the whole output
 
     # cuBLAS BF16 on the same GPU and inputs (context, not the product)
     for _ in range(3):
@@ -438,7 +439,8 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
                         "tflops": round(flops / (cublas_ms * 1e-3) / 1e12, 1),
                         "speedup": round(cublas_ms / ms_per_step, 3)},
         "accuracy": {"rel_l2_vs_fp64": rel, "native_bf16_rel_l2": native_rel,
-                     "ratio": rel / native_rel if native_rel else None, "sampled_rows": int(rows.numel())},
+                     "ratio": rel / native_rel if native_rel else None, "sampled_rows": int(rows.numel()),
+                     "nonfinite_outputs": nonfinite},
         "e2e": {"value": round(job_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": ("RowShardedLinear (gather)" if shard else
