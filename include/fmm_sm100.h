@@ -96,6 +96,16 @@ int fmm_transform_a(int scheme, int dtype, const void* A, int64_t M, int64_t K, 
 int fmm_transform_w(int scheme, int dtype, const void* W, int64_t N, int64_t K, int64_t ldw,
                     void* Rt, fmm_stream_t stream);
 
+/* fmm_transform_a and fmm_transform_w of one dynamic linear in a single
+ * launch (the two input-side transforms share the GPU instead of running
+ * back to back): A[M,K] -> L and weight[N,K] -> Rt, same layouts and
+ * numerics as the two calls.  Replaces the consecutive left_transform_kernel
+ * and right_transform_weight_kernel launches of src/rdna3_fastmm/linear.py:84-115
+ * (src/rdna3_fastmm/runtime.py:597-655); fmm_linear uses it for a native
+ * [N, K] weight. */
+int fmm_transform_aw(int scheme, int dtype, const void* A, int64_t M, int64_t K, int64_t lda,
+                     void* L, const void* W, int64_t N, int64_t ldw, void* Rt, fmm_stream_t stream);
+
 /* Contiguous right matrix B[K,N] (dtype, ldb) -> Rt[R][bn][ldk] (FP16), the
  * same planes as fmm_transform_w of weight = B^T (transposed on chip).  The
  * plain-mm API, per call and for pack_right.

@@ -190,21 +190,62 @@ int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int 
   return static_cast<int>(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 
+template <int SCHEME>
+TransformArgs transform_args(const void* src, int64_t rows, int64_t cols, int64_t ld, void* dst,
+                             int64_t brows, int64_t bcols, int64_t ldd) {
+  using T = SchemeTraits<SCHEME>;
+  const bool vec = (bcols % T::VEC == 0) && (ld % T::VEC == 0) && aligned(src, 2 * T::VEC);
+  TransformArgs a;
+  a.src = static_cast<const uint16_t*>(src);
+  a.rows = rows;
+  a.cols = cols;
+  a.ld = ld;
+  a.dst = static_cast<__half*>(dst);
+  a.brows = brows;
+  a.bcols = bcols;
+  a.ldd = ldd;
+  a.vector_loads = vec ? 1 : 0;
+  return a;
+}
+
 template <int SCHEME, bool kWeight, bool kHalf>
 int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t ld, void* dst,
                            int64_t brows, int64_t bcols, int64_t ldd, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
-  const bool vec = (bcols % T::VEC == 0) && (ld % T::VEC == 0) && aligned(src, 2 * T::VEC);
+  const TransformArgs a = transform_args<SCHEME>(src, rows, cols, ld, dst, brows, bcols, ldd);
   const int64_t items = brows * (ldd / T::VEC);
   using Prog = typename std::conditional<kWeight, typename T::Right, typename T::Left>::type;
   block_transform_kernel<Prog, T::S, T::VEC, kWeight, T::kInThreads, T::kInBlocks, kHalf>
-      <<<streaming_grid(info, items, T::kInThreads, T::kInGrid), T::kInThreads, 0, stream>>>(
-          static_cast<const uint16_t*>(src), rows, cols, ld, static_cast<__half*>(dst), brows,
-          bcols, ldd, vec ? 1 : 0);
+      <<<streaming_grid(info, items, T::kInThreads, T::kInGrid), T::kInThreads, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, kWeight ? "weight transform launch" : "left transform launch");
+  return FMM_OK;
+}
+
+// Left and weight transform of a dynamic linear in one launch; each gets a
+// share of the CTAs proportional to its vectors (at least one).
+template <int SCHEME, bool kHalf>
+int launch_paired_transform(const void* A, int64_t M, int64_t K, int64_t lda, void* L, const void* W,
+                            int64_t N, int64_t ldw, void* Rt, const fmm_dims& d, cudaStream_t stream) {
+  using T = SchemeTraits<SCHEME>;
+  DeviceInfo* info = nullptr;
+  if (int rc = device_info(&info)) return rc;
+  const TransformArgs left = transform_args<SCHEME>(A, M, K, lda, L, d.bm, d.bk, d.ldk);
+  const TransformArgs weight = transform_args<SCHEME>(W, N, K, ldw, Rt, d.bn, d.bk, d.ldk);
+  const int64_t left_items = d.bm * (d.ldk / T::VEC);
+  const int64_t weight_items = d.bn * (d.ldk / T::VEC);
+  int total = streaming_grid(info, left_items + weight_items, T::kInThreads, T::kInGrid);
+  if (total < 2) total = 2;
+  int64_t left_blocks = (int64_t(total) * left_items) / (left_items + weight_items);
+  if (left_blocks < 1) left_blocks = 1;
+  if (left_blocks > total - 1) left_blocks = total - 1;
+  paired_transform_kernel<typename T::Left, typename T::Right, T::S, T::VEC, T::kInThreads,
+                          T::kInBlocks, kHalf>
+      <<<total, T::kInThreads, 0, stream>>>(left, weight, static_cast<uint32_t>(left_blocks));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "paired transform launch");
   return FMM_OK;
 }
 
@@ -299,6 +340,13 @@ struct LeftOp {
   static int run(const void* A, int64_t M, int64_t K, int64_t lda, void* L, const fmm_dims* d,
                  cudaStream_t s) {
     return launch_input_transform<SC, false, H>(A, M, K, lda, L, d->bm, d->bk, d->ldk, s);
+  }
+};
+template <int SC, bool H>
+struct PairedOp {
+  static int run(const void* A, int64_t M, int64_t K, int64_t lda, void* L, const void* W, int64_t N,
+                 int64_t ldw, void* Rt, const fmm_dims* d, cudaStream_t s) {
+    return launch_paired_transform<SC, H>(A, M, K, lda, L, W, N, ldw, Rt, *d, s);
   }
 };
 template <int SC, bool H>
@@ -662,6 +710,20 @@ int fmm_transform_w(int scheme, int dtype, const void* W, int64_t N, int64_t K, 
   return dispatch<WeightOp>(scheme, dtype, W, N, K, ldw, Rt, &d, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int fmm_transform_aw(int scheme, int dtype, const void* A, int64_t M, int64_t K, int64_t lda,
+                     void* L, const void* W, int64_t N, int64_t ldw, void* Rt, fmm_stream_t stream) {
+  fmm_dims d;
+  if (int rc = dims_for(scheme, M, K, N, &d)) return rc;
+  if (int rc = check_dtype(dtype)) return rc;
+  if (A == nullptr || L == nullptr || W == nullptr || Rt == nullptr)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  if (lda < K || ldw < K) return fail(FMM_ERR_INVALID_ARGUMENT, "lda or ldw < K");
+  if (!aligned(L, 16) || !aligned(Rt, 16))
+    return fail(FMM_ERR_MISALIGNED, "L and Rt must be 16-byte aligned");
+  return dispatch<PairedOp>(scheme, dtype, A, M, K, lda, L, W, N, ldw, Rt, &d,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
 int fmm_transform_b(int scheme, int dtype, const void* B, int64_t K, int64_t N, int64_t ldb,
                     void* Rt, fmm_stream_t stream) {
   fmm_dims d;
@@ -723,11 +785,14 @@ int fmm_linear(int scheme, int dtype, const void* A, const void* W, const void* 
     return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
   const bool prepacked = (flags & FMM_LINEAR_PREPACKED) != 0;
   if (!prepacked && W == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null weight");
-  if (int rc = fmm_transform_a(scheme, dtype, A, M, K, K, L, stream)) return rc;
-  if (!prepacked) {
-    const int rc = (flags & FMM_RIGHT_KN) ? fmm_transform_b(scheme, dtype, W, K, N, N, Rt, stream)
-                                          : fmm_transform_w(scheme, dtype, W, N, K, K, Rt, stream);
-    if (rc) return rc;
+  if (!prepacked && !(flags & FMM_RIGHT_KN)) {
+    // native [N, K] weight: both input-side transforms in one launch
+    if (int rc = fmm_transform_aw(scheme, dtype, A, M, K, K, L, W, N, K, Rt, stream)) return rc;
+  } else {
+    if (int rc = fmm_transform_a(scheme, dtype, A, M, K, K, L, stream)) return rc;
+    if (!prepacked) {
+      if (int rc = fmm_transform_b(scheme, dtype, W, K, N, N, Rt, stream)) return rc;
+    }
   }
   if (int rc = fmm_leaf_gemm(static_cast<int>(d.rank), L, Rt, d.bm, d.bn, d.bk, P, stream)) return rc;
   return fmm_reconstruct(scheme, dtype, P, M, N, bias, C, N, stream);

@@ -169,17 +169,29 @@ __device__ __forceinline__ void store_out_vec(uint16_t* p, const VecF<N>& x) {
 // as it needs them.  This memory-level parallelism is what keeps the rank-48/49
 // transforms near HBM bandwidth.  Columns in [bcols, ldd) are padding and are
 // written as zeros.
-template <class Prog, int S, int VEC, bool kWeight, int THREADS = 256, int MIN_BLOCKS = 1,
-          bool kHalfIn = false>
-__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
-    const uint16_t* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
-    __half* __restrict__ dst, int64_t brows, int64_t bcols, int64_t ldd, int vector_loads) {
+struct TransformArgs {
+  const uint16_t* src;
+  int64_t rows, cols, ld;
+  __half* dst;
+  int64_t brows, bcols, ldd;
+  int vector_loads;
+};
+
+// Body shared by the single and the paired launch: `block` / `blocks` are the
+// CTA index and count this transform owns.
+template <class Prog, int S, int VEC, bool kWeight, bool kHalfIn>
+__device__ __forceinline__ void block_transform_body(const TransformArgs& a, uint32_t block,
+                                                     uint32_t blocks) {
   using Raw = typename VecIO<VEC>::BF;
+  const uint16_t* __restrict__ src = a.src;
+  __half* __restrict__ dst = a.dst;
+  const int64_t rows = a.rows, cols = a.cols, ld = a.ld;
+  const int64_t brows = a.brows, bcols = a.bcols, ldd = a.ldd;
+  const int vector_loads = a.vector_loads;
   const int64_t plane = brows * ldd;
   const uint32_t vecs_per_row = static_cast<uint32_t>(ldd / VEC);
   const uint32_t total = static_cast<uint32_t>(brows) * vecs_per_row;
-  for (uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += gridDim.x * blockDim.x) {
+  for (uint32_t idx = block * blockDim.x + threadIdx.x; idx < total; idx += blocks * blockDim.x) {
     const uint32_t i = idx / vecs_per_row;
     const int64_t j = static_cast<int64_t>(idx - i * vecs_per_row) * VEC;
     Raw raw[Prog::kInputs];
@@ -215,6 +227,28 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(
       store_half_vec<VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
     };
     Prog::template run<VecF<VEC>>(in, out);
+  }
+}
+
+template <class Prog, int S, int VEC, bool kWeight, int THREADS = 256, int MIN_BLOCKS = 1,
+          bool kHalfIn = false>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(const TransformArgs a) {
+  block_transform_body<Prog, S, VEC, kWeight, kHalfIn>(a, blockIdx.x, gridDim.x);
+}
+
+// The activation-side and the weight-side transform of one dynamic linear in
+// a single launch: CTAs [0, left_blocks) run the left transform, the rest the
+// weight transform.  Both stream HBM; sharing a launch lets the small left
+// transform's ramp and tail overlap the weight transform instead of
+// serialising with it.
+template <class Left, class Right, int S, int VEC, int THREADS, int MIN_BLOCKS, bool kHalfIn>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) paired_transform_kernel(
+    const TransformArgs left, const TransformArgs weight, uint32_t left_blocks) {
+  if (blockIdx.x < left_blocks) {
+    block_transform_body<Left, S, VEC, false, kHalfIn>(left, blockIdx.x, left_blocks);
+  } else {
+    block_transform_body<Right, S, VEC, true, kHalfIn>(weight, blockIdx.x - left_blocks,
+                                                       gridDim.x - left_blocks);
   }
 }
 

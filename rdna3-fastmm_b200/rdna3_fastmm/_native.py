@@ -58,6 +58,9 @@ _SIGNATURES = {
     "fmm_transform_w": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_transform_b": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_leaf_gemm": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_transform_aw": (
+        [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P], ctypes.c_int,
+    ),
     "fmm_reconstruct": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _P, _P, _I64, _P], ctypes.c_int),
     "fmm_reconstruct_gather": (
         [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _P, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
@@ -147,6 +150,15 @@ def transform_w(scheme: str, W, Rt) -> None:
     N, K = W.shape
     check(library().fmm_transform_w(SCHEME_IDS[scheme], dtype_id(W.dtype), _ptr(W), N, K, W.stride(0),
                                     _ptr(Rt), _stream(W.device)), "fmm_transform_w")
+
+
+def transform_aw(scheme: str, A, L, W, Rt) -> None:
+    """Both input-side transforms of a dynamic linear in one launch."""
+    M, K = A.shape
+    N = W.shape[0]
+    check(library().fmm_transform_aw(SCHEME_IDS[scheme], dtype_id(A.dtype), _ptr(A), M, K, A.stride(0),
+                                     _ptr(L), _ptr(W), N, W.stride(0), _ptr(Rt), _stream(A.device)),
+          "fmm_transform_aw")
 
 
 def transform_b(scheme: str, B, Rt) -> None:

@@ -59,6 +59,24 @@ def test_transforms_match_oracle_bitwise(name, shape):
     assert torch.all(L[:, :, bk:] == 0) and torch.all(Rt[:, :, bk:] == 0)
 
 
+@pytest.mark.parametrize("name", list(PLANS))
+@pytest.mark.parametrize("shape", SHAPES + [(4096, 512, 2048)], ids=lambda s: "x".join(map(str, s)))
+def test_paired_transform_matches_the_two_launches(name, shape):
+    """fmm_transform_aw (one launch) writes the same planes as fmm_transform_a +
+    fmm_transform_w."""
+    M, K, N = shape
+    A, W, _ = make_linear_inputs(M, K, N, seed=0)
+    s, L1, R1, _ = _planes(PLANS[name], M, K, N)
+    _, L2, R2, _ = _planes(PLANS[name], M, K, N)
+    Ad, Wd = A.cuda(), W.cuda()
+    _native.transform_a(name, Ad, L1)
+    _native.transform_w(name, Wd, R1)
+    _native.transform_aw(name, Ad, L2, Wd, R2)
+    torch.cuda.synchronize()
+    assert torch.equal(L1.view(torch.int16), L2.view(torch.int16))
+    assert torch.equal(R1.view(torch.int16), R2.view(torch.int16))
+
+
 def test_weight_transform_handles_full_size_rows():
     """Config-1 size, rank 7: vector fast path over long rows."""
     A, W, _ = make_linear_inputs(512, 1024, 1024, seed=0)
