@@ -198,7 +198,7 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         if args.transport == "p2p":
             description += (f"; rows sharded block-cyclically over {world} GPUs in {args.chunks} chunks, "
                             f"output gathered by the reconstruct kernel itself (stores into every "
-                            f"rank's symmetric buffer over NVLink), overlapped with compute")
+                            f"rank's peer-mapped buffer over NVLink), overlapped with compute")
         else:
             description += (f"; rows sharded block-cyclically over {world} GPUs in {args.chunks} chunks, "
                             f"output all-gathered (NCCL) chunk by chunk, overlapped with compute")
@@ -369,6 +369,8 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     if world > 1:
         dist.all_reduce(local, op=dist.ReduceOp.MAX)
     total_ms, e2e_ms = float(local[0]), float(local[1])
+    if shard:
+        layer.close()  # collective: unmaps the peers' gather buffers (p2p)
     if rank != 0:
         return None
 
@@ -486,7 +488,7 @@ def main() -> None:
                              "all-gather or the gathering reconstruct of the previous chunk")
     parser.add_argument("--transport", choices=("nccl", "p2p"), default="nccl",
                         help="--shard gather: NCCL all-gather, or the reconstruct kernel storing "
-                             "into every rank's symmetric buffer over NVLink")
+                             "into every rank's peer-mapped buffer over NVLink")
     parser.add_argument("--profile", action="store_true",
                         help="timed steps only: no cuBLAS, e2e, parity or CPU legs")
     args = parser.parse_args()

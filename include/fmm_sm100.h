@@ -130,7 +130,7 @@ int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, 
 /* Row-sharded linear, output transform fused with the all-gather: like
  * fmm_reconstruct, but every output element is stored into all `ndest`
  * destinations (1..8) at once -- this rank's own gather buffer and the
- * peers' buffers mapped into this process (CUDA peer / symmetric-memory
+ * peers' buffers mapped into this process (CUDA IPC peer
  * pointers reached over NVLink), each pointing at this rank's first row of
  * the gathered [rows, N] output, with leading dimension `ldc`.  The stores
  * end with a system-scope fence; the caller signals peers (a barrier on the
@@ -141,6 +141,17 @@ int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, 
 int fmm_reconstruct_gather(int scheme, int dtype, const void* P, int64_t M, int64_t N,
                            const void* bias, void* const* dests, int ndest, int64_t ldc,
                            fmm_stream_t stream);
+
+/* Peer memory for fmm_reconstruct_gather, by CUDA IPC (plain peer mappings,
+ * no multicast object): export writes the 64-byte IPC handle of the
+ * allocation containing `ptr` and ptr's byte offset inside it; another
+ * process imports it (peer access enabled on first use) and receives the
+ * mapping's base (for fmm_ipc_close) and the address at `offset`.  No
+ * reference counterpart (the reference is single-GPU). */
+#define FMM_IPC_HANDLE_BYTES 64
+int fmm_ipc_export(const void* ptr, unsigned char* handle, uint64_t* offset);
+int fmm_ipc_import(const unsigned char* handle, uint64_t offset, void** base, void** ptr);
+int fmm_ipc_close(void* base);
 
 /* The whole product through the scheme, using the caller's planes (L, Rt, P
  * sized by fmm_plan_dims): C = A * weight^T (+ bias) for F.linear, or, with

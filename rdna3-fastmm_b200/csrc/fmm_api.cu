@@ -823,6 +823,55 @@ int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bia
                     bytes + left + right, 0u, stream);
 }
 
+// ------------------------------------------------------------------ peer memory (IPC)
+static_assert(sizeof(cudaIpcMemHandle_t) == FMM_IPC_HANDLE_BYTES, "IPC handle size");
+
+int fmm_ipc_export(const void* ptr, unsigned char* handle, uint64_t* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  static PFN_cuMemGetAddressRange_v3020 range = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 3020, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  if (range == nullptr) return fail(FMM_ERR_CUDA, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "pointer is not device memory of this context");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return FMM_OK;
+}
+
+int fmm_ipc_import(const unsigned char* handle, uint64_t offset, void** base, void** ptr) {
+  if (handle == nullptr || base == nullptr || ptr == nullptr)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* mapped = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&mapped, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *base = mapped;
+  *ptr = static_cast<unsigned char*>(mapped) + offset;
+  return FMM_OK;
+}
+
+int fmm_ipc_close(void* base) {
+  if (base == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return FMM_OK;
+}
+
 int fmm_set_sm_budget(int sms) {
   if (sms < 0) return fail(FMM_ERR_INVALID_ARGUMENT, "SM budget must be >= 0");
   g_sm_budget = sms;

@@ -58,6 +58,13 @@ _SIGNATURES = {
     "fmm_transform_w": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_transform_b": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_leaf_gemm": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_ipc_export": ([_P, ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
+    "fmm_ipc_import": (
+        [ctypes.POINTER(ctypes.c_ubyte), ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
+         ctypes.POINTER(ctypes.c_void_p)],
+        ctypes.c_int,
+    ),
+    "fmm_ipc_close": ([_P], ctypes.c_int),
     "fmm_transform_aw": (
         [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P], ctypes.c_int,
     ),
@@ -175,6 +182,29 @@ def leaf_gemm(rank: int, L, Rt, bm: int, bn: int, bk: int, P) -> None:
 def reconstruct(scheme: str, P, M: int, N: int, bias, C) -> None:
     check(library().fmm_reconstruct(SCHEME_IDS[scheme], dtype_id(C.dtype), _ptr(P), M, N, _ptr(bias),
                                     _ptr(C), C.stride(0), _stream(P.device)), "fmm_reconstruct")
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_export(ptr: int) -> tuple[bytes, int]:
+    """(IPC handle bytes, offset) of the device allocation holding ``ptr``."""
+    handle = (ctypes.c_ubyte * IPC_HANDLE_BYTES)()
+    offset = ctypes.c_uint64()
+    check(library().fmm_ipc_export(ptr, handle, ctypes.byref(offset)), "fmm_ipc_export")
+    return bytes(handle), offset.value
+
+
+def ipc_import(handle: bytes, offset: int) -> tuple[int, int]:
+    """Map a peer's exported allocation: (mapping base, address at offset)."""
+    raw = (ctypes.c_ubyte * IPC_HANDLE_BYTES).from_buffer_copy(handle)
+    base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+    check(library().fmm_ipc_import(raw, offset, ctypes.byref(base), ctypes.byref(ptr)), "fmm_ipc_import")
+    return int(base.value), int(ptr.value)
+
+
+def ipc_close(base: int) -> None:
+    check(library().fmm_ipc_close(base), "fmm_ipc_close")
 
 
 def reconstruct_gather(scheme: str, P, M: int, N: int, bias, dests: list[int], ldc: int, dtype) -> None:

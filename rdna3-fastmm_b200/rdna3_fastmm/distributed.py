@@ -16,10 +16,10 @@ asynchronously while the next chunk computes, overlapping NVLink traffic with
 tensor-core work.
 
 ``transport="p2p"`` replaces the reconstruct + NCCL all-gather pair by one
-kernel (``fmm_reconstruct_gather``): the gather buffer is symmetric memory
-(``torch.distributed._symmetric_memory``), and each rank's output transform
-stores every output vector into its own buffer and, over NVLink, into every
-peer's buffer at this rank's rows.  With ``chunks > 1`` the gathering
+kernel (``fmm_reconstruct_gather``): every rank exports its gather buffer by
+CUDA IPC and maps its peers' buffers (plain peer mappings, no multicast
+object), and each rank's output transform stores every output vector into its
+own buffer and, over NVLink, into every peer's buffer at this rank's rows.  With ``chunks > 1`` the gathering
 reconstruct of chunk c runs on a side stream while chunk c + 1 transforms and
 multiplies (two product workspaces alternate), so NVLink traffic overlaps
 tensor-core work without reserving SMs for a collective.  A one-element
@@ -109,17 +109,26 @@ class RowShardedLinear:
             self._setup_p2p(max_free_memory_fraction)
 
     def _setup_p2p(self, max_free_memory_fraction: float) -> None:
-        import torch.distributed._symmetric_memory as symm
+        from . import _native
 
         if self.world > 8:
             raise ValueError("the gathering reconstruct stores to at most 8 ranks")
         if self.bias is not None and self.bias.dtype != torch.bfloat16:
             raise ValueError("bias must be BF16")
         # exact [M, N] rows: every rank writes its own rows, no padding slots
-        self._symm_out = symm.empty(self.rows, self.columns, dtype=torch.bfloat16, device=self.device)
-        group = self.group if self.group is not None else dist.group.WORLD
-        self._symm = symm.rendezvous(self._symm_out, group)
-        self._peer_bases = [int(p) for p in self._symm.buffer_ptrs]
+        self._gather_out = torch.empty((self.rows, self.columns), dtype=torch.bfloat16, device=self.device)
+        mine = _native.ipc_export(self._gather_out.data_ptr())
+        exported: list = [None] * self.world
+        dist.all_gather_object(exported, mine, group=self.group)
+        self._ipc_bases: list[int] = []
+        self._peer_bases: list[int] = []
+        for peer, (handle, offset) in enumerate(exported):
+            if peer == self.rank:
+                self._peer_bases.append(self._gather_out.data_ptr())
+            else:
+                base, ptr = _native.ipc_import(handle, offset)
+                self._ipc_bases.append(base)
+                self._peer_bases.append(ptr)
         # a second product workspace so chunk c's gathering reconstruct can
         # read its products while chunk c + 1 multiplies
         self._products = [self.workspace.products]
@@ -127,6 +136,20 @@ class RowShardedLinear:
             self._products.append(torch.empty_like(self.workspace.products))
         self._side = torch.cuda.Stream(device=self.device)
         self._flag = torch.zeros(1, device=self.device, dtype=torch.int32)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (p2p transport).  Collective: no rank frees
+        its gather buffer while a peer could still write into it."""
+        if self.transport != "p2p" or not self._ipc_bases:
+            return
+        from . import _native
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for base in self._ipc_bases:
+            _native.ipc_close(base)
+        self._ipc_bases = []
+        dist.barrier(group=self.group)
 
     def _p2p(self, local_rows: torch.Tensor) -> torch.Tensor:
         main = torch.cuda.current_stream(self.device)
@@ -144,7 +167,7 @@ class RowShardedLinear:
         # a rank only after every rank's kernels (and their fenced peer
         # stores) have finished; NCCL's process-group timeout bounds the wait
         dist.all_reduce(self._flag, group=self.group)
-        return self._symm_out
+        return self._gather_out
 
     def _p2p_chunks(self, local_rows: torch.Tensor, main, row_bytes: int, done: list) -> None:
         from . import _native
@@ -208,7 +231,7 @@ class RowShardedLinear:
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Run this rank's rows; with ``gather`` return the whole ``C[M, N]``
         on every rank, else this rank's ``[count, N]`` rows (local order).
-        With the p2p transport the gathered result is the layer's symmetric
+        With the p2p transport the gathered result is the layer's own gather
         buffer, overwritten by the next call."""
         if tuple(local_rows.shape) != (self.count, self.inner):
             raise ValueError(f"local rows have shape {tuple(local_rows.shape)}, "
@@ -216,7 +239,7 @@ class RowShardedLinear:
         ch = self.chunk_rows
         if gather and self.transport == "p2p":
             if out is not None:
-                raise ValueError("the p2p transport gathers into its own symmetric buffer")
+                raise ValueError("the p2p transport gathers into its own peer-mapped buffer")
             return self._p2p(local_rows)
         if not gather:
             result = out if out is not None else torch.empty(
