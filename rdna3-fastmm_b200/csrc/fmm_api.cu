@@ -152,7 +152,7 @@ struct SchemeTraits<FMM_SCHEME_RANK48> {
   static constexpr int S = 4;
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
-  static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 64;
+  static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 16;
   static constexpr bool kTensorCoreOutput = false;
   static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
 };

@@ -160,3 +160,44 @@ def test_compiled_model_runs_through_the_backend():
 def test_memory_guard_blocks_rewrite(monkeypatch):
     monkeypatch.setattr(torch.cuda, "mem_get_info", lambda device=None: (1024, 2**34))
     assert not linear_module._has_linear_memory_budget(Rank7Plan, (4096, 4096, 4096), DEVICE)
+
+
+@pytest.mark.parametrize("plan_type", PLANS)
+@pytest.mark.parametrize("prepacked", [False, True])
+def test_linear_captures_into_a_cuda_graph(plan_type, prepacked):
+    """After one eager call (which sets kernel attributes), a plan call is
+    stream-ordered, synchronisation- and allocation-free, so it captures into a
+    CUDA graph; replays give the eager bits for new inputs copied in place."""
+    M, K, N = 520, 384, 776
+    A, W, bias = make_linear_inputs(M, K, N, seed=0, bias=True)
+    A2 = make_linear_inputs(M, K, N, seed=5)[0]
+    plan = _plan(plan_type, M, K, N)
+    x, w, b = A.to(DEVICE), W.to(DEVICE), bias.to(DEVICE)
+    out = torch.empty((M, N), device=DEVICE, dtype=torch.bfloat16)
+    if prepacked:
+        packed = plan.pack_weight(w, 0.5)
+        ws = plan.allocate_workspace(0.5, prepacked_right=True)
+        call = lambda: plan.run_linear_packed(x, packed, ws, b, out)  # noqa: E731
+    else:
+        ws = plan.allocate_workspace(0.5)
+        call = lambda: plan.run_linear(x, w, ws, b, out)  # noqa: E731
+    call()
+    torch.cuda.synchronize()
+    expected_first = out.clone()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        call()  # warm the side stream once, as torch.cuda.graph expects
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        call()
+    out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), expected_first.view(torch.int16))
+    x.copy_(A2.to(DEVICE))
+    graph.replay()
+    torch.cuda.synchronize()
+    eager = (plan.run_linear_packed(x, packed, ws, b) if prepacked else plan.run_linear(x, w, ws, b))
+    assert torch.equal(out.view(torch.int16), eager.view(torch.int16))
