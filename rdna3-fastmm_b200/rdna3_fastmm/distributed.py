@@ -26,8 +26,8 @@ tensor-core work without reserving SMs for a collective.  A one-element
 all-reduce queued behind the kernels makes every peer's rows visible before
 the result is used.
 
-The reference is single-GPU; this is the multi-GPU form north_star asks for
-(M sharded across 1/2/4/8 GPUs, weight replicated, all-gather on demand).
+The reference is single-GPU; this is the path's multi-GPU form (M sharded
+across 1/2/4/8 GPUs, weight replicated, output gathered on demand).
 """
 
 from __future__ import annotations
