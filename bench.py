@@ -481,8 +481,10 @@ def main() -> None:
                         help="override M (smaller cases for profiler captures)")
     parser.add_argument("--shard", action="store_true",
                         help="split M over the ranks and all-gather C (strong scaling)")
-    parser.add_argument("--chunks", type=int, default=4,
-                        help="row chunks per rank in --shard mode (gather overlaps compute)")
+    parser.add_argument("--chunks", type=int, default=None,
+                        help="row chunks per rank in --shard mode (default: 4 with the NCCL gather, "
+                             "which overlaps the next chunk; 1 with --transport p2p, whose gathering "
+                             "reconstruct is already NVLink-bound)")
     parser.add_argument("--reserve-sms", type=int, default=32,
                         help="SMs the GEMM leaves free, while --shard chunks compute, for the NCCL "
                              "all-gather or the gathering reconstruct of the previous chunk")
@@ -493,6 +495,8 @@ def main() -> None:
                         help="timed steps only: no cuBLAS, e2e, parity or CPU legs")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.chunks is None:
+        args.chunks = 1 if args.transport == "p2p" else 4
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
