@@ -67,3 +67,41 @@ def test_host_side_errors_need_no_gpu():
 
 def test_version():
     assert _native.library().fmm_version() >= 100
+
+
+def test_rank343_plan_dims():
+    d = _native.plan_dims("rank343", 16384, 16384, 16384)
+    assert (d.scheme_size, d.rank, d.bm, d.bk, d.bn) == (8, 343, 2048, 2048, 2048)
+    assert d.left_elements == 343 * 2048 * 2048
+    m = MatrixShape.from_dimensions(67, 71, 73, 8)
+    d = _native.plan_dims("rank343", 67, 71, 73)
+    assert (d.bm, d.bk, d.bn, d.ldk, d.ldp) == (m.block_rows, m.block_inner, m.block_columns,
+                                                m.inner_pitch, m.column_pitch)
+
+
+def test_newer_entry_points_validate_on_the_host():
+    lib = _native.library()
+    fake = ctypes.c_void_p(0x1000)
+    # paired transform: null operands, short leading dimension, misaligned planes
+    assert lib.fmm_transform_aw(7, 0, None, 4, 4, 4, fake, fake, 4, 4, fake, None) == \
+        _native.FMM_ERR_INVALID_ARGUMENT
+    assert lib.fmm_transform_aw(7, 0, fake, 4, 8, 4, fake, fake, 4, 8, fake, None) == \
+        _native.FMM_ERR_INVALID_ARGUMENT
+    odd = ctypes.c_void_p(0x1002)
+    assert lib.fmm_transform_aw(7, 0, fake, 4, 4, 4, odd, fake, 4, 4, fake, None) == \
+        _native.FMM_ERR_MISALIGNED
+    # gathering reconstruct: destination count and pointers
+    dests = (ctypes.c_void_p * 9)(*([0x1000] * 9))
+    for ndest in (0, 9):
+        assert lib.fmm_reconstruct_gather(48, 0, fake, 8, 8, None, dests, ndest, 8, None) == \
+            _native.FMM_ERR_INVALID_ARGUMENT
+    assert "ndest" in _native.last_error()
+    nulls = (ctypes.c_void_p * 2)(0x1000, None)
+    assert lib.fmm_reconstruct_gather(48, 0, fake, 8, 8, None, nulls, 2, 8, None) == \
+        _native.FMM_ERR_INVALID_ARGUMENT
+    # rank 343 is FP16 only and has no gathering reconstruct
+    assert lib.fmm_transform_a(343, 0, fake, 16, 16, 16, fake, None) == _native.FMM_ERR_UNSUPPORTED
+    assert "FP16" in _native.last_error()
+    # IPC: null arguments are refused before any driver call
+    assert lib.fmm_ipc_export(None, None, None) == _native.FMM_ERR_INVALID_ARGUMENT
+    assert lib.fmm_ipc_close(None) == _native.FMM_ERR_INVALID_ARGUMENT
