@@ -142,7 +142,7 @@ struct SchemeTraits<FMM_SCHEME_RANK7> {
   static constexpr int kInThreads = 256, kInBlocks = 1, kInGrid = 64;
   static constexpr int kOutVec = 8, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 64;
   static constexpr bool kTensorCoreOutput = false;
-  static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
+  static constexpr int kKnTK = 64, kKnTN = 32, kKnVec = 4, kKnThreads = 256, kKnBlocks = 4;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK48> {
@@ -154,7 +154,7 @@ struct SchemeTraits<FMM_SCHEME_RANK48> {
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 16;
   static constexpr bool kTensorCoreOutput = false;
-  static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
+  static constexpr int kKnTK = 64, kKnTN = 32, kKnVec = 2, kKnThreads = 256, kKnBlocks = 2;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK49> {
@@ -166,7 +166,7 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 64;
   static constexpr bool kTensorCoreOutput = false;
-  static constexpr int kKnTile = 32, kKnVec = 4, kKnThreads = 256;
+  static constexpr int kKnTK = 64, kKnTN = 32, kKnVec = 2, kKnThreads = 256, kKnBlocks = 2;
 };
 // Rank 343: 64 inputs and 343 planes per position.  The input side keeps two
 // elements per thread (64 packed inputs plus the circuit fit in registers);
@@ -181,7 +181,7 @@ struct SchemeTraits<FMM_SCHEME_RANK343> {
   static constexpr int VEC = 2;
   static constexpr int kInThreads = 128, kInBlocks = 1, kInGrid = 16;
   static constexpr bool kTensorCoreOutput = true;
-  static constexpr int kKnTile = 16, kKnVec = 2, kKnThreads = 128;
+  static constexpr int kKnTK = 32, kKnTN = 16, kKnVec = 2, kKnThreads = 128, kKnBlocks = 1;
 };
 
 int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int blocks_per_sm) {
@@ -303,16 +303,29 @@ int launch_reconstruct_gather(const void* P, const fmm_dims& d, int64_t M, int64
   }
 }
 
+template <class Kernel>
+int ensure_smem_attribute(bool& done, Kernel kernel, size_t bytes);
+
 template <int SCHEME, bool kHalf>
 int launch_right_kn(const void* B, int64_t K, int64_t N, int64_t ldb, void* dst, const fmm_dims& d,
                     cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
-  constexpr int kTile = T::kKnTile;
-  const dim3 grid(static_cast<unsigned>(ceil_div(d.ldk, kTile)),
-                  static_cast<unsigned>(ceil_div(d.bn, kTile)));
-  right_transform_kn_kernel<typename T::Right, T::S, kHalf, kTile, T::kKnVec>
-      <<<grid, T::kKnThreads, 0, stream>>>(static_cast<const uint16_t*>(B), K, N, ldb,
-                                           static_cast<__half*>(dst), d.bk, d.bn, d.ldk);
+  constexpr int TK = T::kKnTK, TN = T::kKnTN;
+  using Tile = KnTile<T::S, TK, TN>;
+  auto kernel = right_transform_kn_kernel<typename T::Right, T::S, kHalf, TK, TN, T::kKnVec, T::kKnThreads,
+                                           T::kKnBlocks>;
+  static bool configured[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (Tile::kBytes > 48 * 1024 && dev >= 0 && dev < kMaxDevices) {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (int rc = ensure_smem_attribute(configured[dev], kernel, Tile::kBytes)) return rc;
+  }
+  const dim3 grid(static_cast<unsigned>(ceil_div(d.ldk, TK)), static_cast<unsigned>(ceil_div(d.bn, TN)));
+  const bool vec = (ldb % 8 == 0) && (d.bn % 8 == 0) && aligned(B, 16);
+  kernel<<<grid, T::kKnThreads, Tile::kBytes, stream>>>(static_cast<const uint16_t*>(B), K, N, ldb,
+                                                        static_cast<__half*>(dst), d.bk, d.bn, d.ldk,
+                                                        vec ? 1 : 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "right transform (K x N) launch");
   return FMM_OK;

@@ -406,41 +406,73 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_gather_kernel
 // ---------------------------------------------------------------------------
 // Right transform of a contiguous B[K, N] (the plain-mm API): the program's
 // input q is block (q / S, q % S) of B and the planes come out K-major,
-// Rt[r][n][k], so each block is transposed on the way.  A CTA owns one
-// TILE x TILE position (k0, n0) inside the blocks: it stages the S*S input
-// tiles in shared memory with row loads along n (coalesced), then each thread
-// evaluates the program for VEC consecutive k at one n, reading the staged
-// tiles down a column, and stores VEC elements along k (coalesced).
-template <class Prog, int S, bool kHalfIn, int TILE = 32, int VEC = 4>
-__global__ void __launch_bounds__(256) right_transform_kn_kernel(
+// Rt[r][n][k], so each block is transposed on the way.  A CTA owns TK x TN
+// positions (k0.., n0..) inside the blocks.
+//   load:    the S*S input tiles are read with lanes along n (each B row
+//            segment is contiguous) and written to shared memory transposed,
+//            tile[q][n][k], rows padded by 2 elements against bank conflicts;
+//   compute: each thread takes VEC consecutive k at one n -- one vector read
+//            per input from shared memory -- and stores VEC elements of every
+//            output plane; the lanes of a warp cover TK / VEC consecutive
+//            vectors of one n, so each plane store is one contiguous run of
+//            2*TK bytes.
+// Shared memory: S*S * TN * (TK + 2) * 2 bytes (dynamic).
+template <int S, int TK, int TN>
+struct KnTile {
+  static constexpr int kQ = S * S;
+  static constexpr int kPitch = TK + 2;
+  static constexpr size_t kBytes = size_t(kQ) * TN * kPitch * 2;
+};
+
+template <class Prog, int S, bool kHalfIn, int TK, int TN, int VEC, int THREADS, int MIN_BLOCKS>
+__global__ void __launch_bounds__(THREADS, MIN_BLOCKS) right_transform_kn_kernel(
     const uint16_t* __restrict__ B, int64_t K, int64_t N, int64_t ldb, __half* __restrict__ dst,
-    int64_t bk, int64_t bn, int64_t ldk) {
-  constexpr int Q = S * S;
-  __shared__ uint16_t tile[Q][TILE][TILE + 2];
-  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * TILE;
-  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * TILE;
-  for (int idx = threadIdx.x; idx < Q * TILE * TILE; idx += blockDim.x) {
-    const int q = idx / (TILE * TILE);
-    const int kk = (idx / TILE) % TILE;
-    const int nn = idx % TILE;
+    int64_t bk, int64_t bn, int64_t ldk, int vector_loads) {
+  using T = KnTile<S, TK, TN>;
+  static_assert(TN % 8 == 0, "16-byte source chunks");
+  extern __shared__ uint16_t kn_tile[];  // [kQ][TN][kPitch]
+  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * TK;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * TN;
+  // 16-byte chunks of 8 consecutive n; a chunk whose source row is in range
+  // and whose 8 columns all lie inside the block (and B) is one vector load,
+  // anything else goes element by element with zero padding
+  constexpr int kChunks = TN / 8;
+  for (int idx = threadIdx.x; idx < T::kQ * TK * kChunks; idx += THREADS) {
+    const int q = idx / (TK * kChunks);
+    const int kk = (idx / kChunks) % TK;
+    const int nn = (idx % kChunks) * 8;
     const int64_t k = k0 + kk, n = n0 + nn;
     const int64_t row = (q / S) * bk + k, col = (q % S) * bn + n;
-    const bool ok = k < bk && n < bn && row < K && col < N;
-    tile[q][kk][nn] = ok ? B[row * ldb + col] : uint16_t(0);
+    uint16_t* to = kn_tile + (q * TN + nn) * T::kPitch + kk;
+    if (vector_loads && k < bk && row < K && n + 8 <= bn && col + 8 <= N) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(B + row * ldb + col));
+      const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) to[t * T::kPitch] = e[t];
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const bool ok = k < bk && n + t < bn && row < K && col + t < N;
+        to[t * T::kPitch] = ok ? B[row * ldb + col + t] : uint16_t(0);
+      }
+    }
   }
   __syncthreads();
   const int64_t plane = bn * ldk;
-  constexpr int kVecsPerColumn = TILE / VEC;
-  for (int idx = threadIdx.x; idx < TILE * kVecsPerColumn; idx += blockDim.x) {
-    const int nn = idx / kVecsPerColumn;
-    const int kk = (idx % kVecsPerColumn) * VEC;
+  constexpr int kVecs = TK / VEC;  // vectors along k per n
+  using Raw = typename VecIO<VEC>::BF;
+  for (int idx = threadIdx.x; idx < TN * kVecs; idx += THREADS) {
+    const int nn = idx / kVecs;
+    const int kk = (idx % kVecs) * VEC;
     const int64_t n = n0 + nn, k = k0 + kk;
     if (n >= bn || k >= ldk) continue;
     auto in = [&](int q) -> VecF<VEC> {
-      VecF<VEC> x;
+      Raw raw;
+      uint16_t* e = reinterpret_cast<uint16_t*>(&raw);
+      const uint16_t* src = kn_tile + (q * TN + nn) * T::kPitch + kk;
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) x.v[e] = widen_in<kHalfIn>(tile[q][kk + e][nn]);
-      return x;
+      for (int v = 0; v < VEC; ++v) e[v] = src[v];
+      return unpack_in<kHalfIn, VEC>(raw);
     };
     auto out = [&](int o, const VecF<VEC>& x) {
       store_half_vec<VEC>(dst + o * plane + n * ldk + k, x);
