@@ -129,7 +129,10 @@ int usable_sms(const DeviceInfo* info) {
 // ------------------------------------------------------------------ dispatch
 // Launch shapes were swept on B200 with random data (threads per block,
 // minimum resident blocks, grid cap in blocks per SM); with every input
-// preloaded these reach 91-98 % of the measured copy bandwidth.
+// preloaded these reach 91-98 % of the measured copy bandwidth.  The K x N
+// right transform (plain-mm API) was swept separately: small 32 (k) x 8 (n)
+// tiles with two k per thread and many resident blocks won for every scheme
+// (16384^2: rank 7 4.8, rank 48/49 4.2, rank 343 2.4 TB/s).
 template <int SCHEME>
 struct SchemeTraits;
 template <>
@@ -142,7 +145,7 @@ struct SchemeTraits<FMM_SCHEME_RANK7> {
   static constexpr int kInThreads = 256, kInBlocks = 1, kInGrid = 64;
   static constexpr int kOutVec = 8, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 64;
   static constexpr bool kTensorCoreOutput = false;
-  static constexpr int kKnTK = 64, kKnTN = 32, kKnVec = 4, kKnThreads = 256, kKnBlocks = 4;
+  static constexpr int kKnTK = 32, kKnTN = 8, kKnVec = 2, kKnThreads = 128, kKnBlocks = 4;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK48> {
@@ -154,7 +157,7 @@ struct SchemeTraits<FMM_SCHEME_RANK48> {
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 16;
   static constexpr bool kTensorCoreOutput = false;
-  static constexpr int kKnTK = 64, kKnTN = 32, kKnVec = 2, kKnThreads = 256, kKnBlocks = 2;
+  static constexpr int kKnTK = 32, kKnTN = 8, kKnVec = 2, kKnThreads = 128, kKnBlocks = 4;
 };
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK49> {
@@ -166,12 +169,12 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 64;
   static constexpr bool kTensorCoreOutput = false;
-  static constexpr int kKnTK = 64, kKnTN = 32, kKnVec = 2, kKnThreads = 256, kKnBlocks = 2;
+  static constexpr int kKnTK = 32, kKnTN = 8, kKnVec = 2, kKnThreads = 128, kKnBlocks = 4;
 };
 // Rank 343: 64 inputs and 343 planes per position.  The input side keeps two
 // elements per thread (64 packed inputs plus the circuit fit in registers);
 // the output side is a tensor-core product with the coefficient matrix
-// (reconstruct_tc.cuh); the K x N right transform stages 64 tiles of 16 x 16.
+// (reconstruct_tc.cuh).
 template <>
 struct SchemeTraits<FMM_SCHEME_RANK343> {
   using Left = gen::Rank343Left;
@@ -181,7 +184,7 @@ struct SchemeTraits<FMM_SCHEME_RANK343> {
   static constexpr int VEC = 2;
   static constexpr int kInThreads = 128, kInBlocks = 1, kInGrid = 16;
   static constexpr bool kTensorCoreOutput = true;
-  static constexpr int kKnTK = 32, kKnTN = 16, kKnVec = 2, kKnThreads = 128, kKnBlocks = 1;
+  static constexpr int kKnTK = 32, kKnTN = 8, kKnVec = 2, kKnThreads = 128, kKnBlocks = 1;
 };
 
 int streaming_grid(const DeviceInfo* info, int64_t work_items, int threads, int blocks_per_sm) {
