@@ -19,6 +19,7 @@
 #include "generated/fmm_schemes.cuh"
 #include "leaf_gemm.cuh"
 #include "reconstruct_tc.cuh"
+#include "reconstruct_staged.cuh"
 
 // Scratch of fmm_linear_noalloc: the L, Rt and P planes of one call live in
 // this array instead of caller-provided buffers.  It is part of the module, so
@@ -132,7 +133,11 @@ int usable_sms(const DeviceInfo* info) {
 // preloaded these reach 91-98 % of the measured copy bandwidth.  The K x N
 // right transform (plain-mm API) was swept separately: small 32 (k) x 8 (n)
 // tiles with two k per thread and many resident blocks won for every scheme
-// (16384^2: rank 7 4.8, rank 48/49 4.2, rank 343 2.4 TB/s).
+// (16384^2: rank 7 4.8, rank 48/49 4.2, rank 343 2.4 TB/s).  The rank-48/49
+// reconstruct runs TMA-staged (kOutStages > 0): timed right after the leaf
+// GEMM that writes its products, 2 stages of 256 positions and 4 CTAs per SM
+// beat the register kernel by 12-25 % (3 stages x 2 CTAs, fewer compute warps
+// per SM, lost to it; 128-position tiles and single stages were slower).
 template <int SCHEME>
 struct SchemeTraits;
 template <>
@@ -144,6 +149,7 @@ struct SchemeTraits<FMM_SCHEME_RANK7> {
   static constexpr int VEC = 8;
   static constexpr int kInThreads = 256, kInBlocks = 1, kInGrid = 64;
   static constexpr int kOutVec = 8, kOutThreads = 128, kOutBlocks = 4, kOutGrid = 64;
+  static constexpr int kOutStages = 0;
   static constexpr bool kTensorCoreOutput = false;
   static constexpr int kKnTK = 32, kKnTN = 8, kKnVec = 2, kKnThreads = 128, kKnBlocks = 4;
 };
@@ -156,6 +162,7 @@ struct SchemeTraits<FMM_SCHEME_RANK48> {
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 16;
+  static constexpr int kOutStages = 2, kOutStagedBlocks = 4;
   static constexpr bool kTensorCoreOutput = false;
   static constexpr int kKnTK = 32, kKnTN = 8, kKnVec = 2, kKnThreads = 128, kKnBlocks = 4;
 };
@@ -168,6 +175,7 @@ struct SchemeTraits<FMM_SCHEME_RANK49> {
   static constexpr int VEC = 4;
   static constexpr int kInThreads = 128, kInBlocks = 4, kInGrid = 64;
   static constexpr int kOutVec = 4, kOutThreads = 128, kOutBlocks = 3, kOutGrid = 64;
+  static constexpr int kOutStages = 2, kOutStagedBlocks = 4;
   static constexpr bool kTensorCoreOutput = false;
   static constexpr int kKnTK = 32, kKnTN = 8, kKnVec = 2, kKnThreads = 128, kKnBlocks = 4;
 };
@@ -257,6 +265,17 @@ int launch_reconstruct_tc(const void* P, const fmm_dims& d, int64_t M, int64_t N
                           void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream);
 
 template <int SCHEME, bool kHalf>
+int launch_reconstruct_staged(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
+                              void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream);
+
+// FMM_RECONSTRUCT_VARIANT=register keeps the circuit schemes on the register
+// reconstruct (the TMA-staged one is the default where a scheme has stages).
+bool staged_reconstruct_enabled() {
+  const char* v = std::getenv("FMM_RECONSTRUCT_VARIANT");
+  return v == nullptr || std::string(v) != "register";
+}
+
+template <int SCHEME, bool kHalf>
 int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                        void* C, int64_t ldc, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
@@ -265,6 +284,10 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
   if constexpr (T::kTensorCoreOutput) {
     return launch_reconstruct_tc<typename T::Output, kHalf>(P, d, M, N, bias, C, ldc, info, stream);
   } else {
+    if constexpr (T::kOutStages > 0) {
+      if (staged_reconstruct_enabled() && aligned(P, 16) && d.ldp % 8 == 0)
+        return launch_reconstruct_staged<SCHEME, kHalf>(P, d, M, N, bias, C, ldc, info, stream);
+    }
     constexpr int V = T::kOutVec;
     const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
     const bool vec_bias = (d.bn % V == 0) && bias != nullptr && aligned(bias, 2 * V);
@@ -440,7 +463,8 @@ int plane_map(CUtensorMap* map, const void* base, int64_t k, int64_t rows, int64
 
 // Generic 3-D FP16 tiled map (128-byte swizzle); strides in bytes.
 int tiled_map_3d(CUtensorMap* map, const void* base, const int64_t (&dims)[3],
-                 const int64_t (&strides)[2], const uint32_t (&box)[3]) {
+                 const int64_t (&strides)[2], const uint32_t (&box)[3],
+                 CUtensorMapSwizzle swizzle) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (int rc = tensor_map_encoder(&encode)) return rc;
   cuuint64_t d[3] = {static_cast<cuuint64_t>(dims[0]), static_cast<cuuint64_t>(dims[1]),
@@ -449,7 +473,7 @@ int tiled_map_3d(CUtensorMap* map, const void* base, const int64_t (&dims)[3],
   cuuint32_t b[3] = {box[0], box[1], box[2]};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), d, st, b,
-                      elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FMM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return FMM_OK;
@@ -574,11 +598,12 @@ int launch_reconstruct_tc(const void* P, const fmm_dims& d, int64_t M, int64_t N
   CUtensorMap map_p, map_w;
   // P[343][bm][ldp] as (position, row, product); box 64 positions x 1 row x 64 products
   if (int rc = tiled_map_3d(&map_p, P, {d.ldp, d.bm, kRcRank}, {d.ldp * 2, d.bm * d.ldp * 2},
-                            {64u, 1u, static_cast<uint32_t>(kRcK)}))
+                            {64u, 1u, static_cast<uint32_t>(kRcK)}, CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   if (int rc = tiled_map_3d(&map_w, info->rank343_wt, {kRcKPadded, kRcN, 1},
                             {int64_t(kRcKPadded) * 2, int64_t(kRcKPadded) * kRcN * 2},
-                            {static_cast<uint32_t>(kRcK), static_cast<uint32_t>(kRcN), 1u}))
+                            {static_cast<uint32_t>(kRcK), static_cast<uint32_t>(kRcN), 1u},
+                            CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   {
     std::lock_guard<std::mutex> lock(g_device_mutex);
@@ -605,6 +630,53 @@ int launch_reconstruct_tc(const void* P, const fmm_dims& d, int64_t M, int64_t N
   reconstruct_tc_kernel<RcCfg, kHalf><<<grid, kRcThreads, RcCfg::kSmemBytes, stream>>>(map_p, map_w, prm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "rank-343 reconstruct launch");
+  return FMM_OK;
+}
+
+// TMA-staged reconstruct of a circuit scheme: persistent CTAs, one box of
+// 256 positions x R products per tile (unswizzled, so plane r of a tile sits at
+// r * 256 elements in shared memory), two positions a compute thread.
+template <int SCHEME, bool kHalf>
+int launch_reconstruct_staged(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
+                              void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream) {
+  using T = SchemeTraits<SCHEME>;
+  using Prog = typename T::Output;
+  using Cfg = StagedReconstructConfig<Prog, T::kOutStages>;
+  auto kernel = reconstruct_staged_kernel<Prog, T::S, T::kOutStages, kHalf, Cfg::kTP, T::kOutStagedBlocks>;
+  static bool configured[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
+  {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (int rc = ensure_smem_attribute(configured[dev], kernel, Cfg::kSmemBytes)) return rc;
+  }
+  CUtensorMap map_p;
+  if (int rc = tiled_map_3d(&map_p, P, {d.ldp, d.bm, int64_t(Cfg::kR)}, {d.ldp * 2, d.bm * d.ldp * 2},
+                            {uint32_t(Cfg::kTP), 1u, uint32_t(Cfg::kR)}, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  StagedReconstructParams prm;
+  prm.bm = d.bm;
+  prm.bn = d.bn;
+  prm.M = M;
+  prm.N = N;
+  prm.ldc = ldc;
+  const int64_t per_row = ceil_div(d.bn, Cfg::kTP);
+  if (d.bm * per_row > 0x7fffffff) return fail(FMM_ERR_TOO_LARGE, "too many reconstruct tiles");
+  prm.tiles_per_row = static_cast<int32_t>(per_row);
+  prm.total_tiles = static_cast<int32_t>(d.bm * per_row);
+  const bool vec = (d.bn % Cfg::kVec == 0) && (ldc % Cfg::kVec == 0) && aligned(C, 2 * Cfg::kVec);
+  const bool vec_bias = (d.bn % Cfg::kVec == 0) && bias != nullptr && aligned(bias, 2 * Cfg::kVec);
+  prm.vector_flags = (vec ? 1 : 0) | (vec_bias ? 2 : 0);
+  prm.bias = static_cast<const uint16_t*>(bias);
+  prm.C = static_cast<uint16_t*>(C);
+  prm.timeout_ns = g_timeout_ns;
+  const int64_t cap = int64_t(usable_sms(info)) * T::kOutStagedBlocks;
+  const int grid = static_cast<int>(prm.total_tiles < cap ? prm.total_tiles : cap);
+  kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(map_p, prm);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "staged reconstruct launch");
   return FMM_OK;
 }
 

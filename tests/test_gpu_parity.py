@@ -89,10 +89,19 @@ def test_weight_transform_handles_full_size_rows():
                                   oracle.weight_transform("rank7", f32(W)).view(np.int16))
 
 
+# The circuit schemes have two reconstruct kernels: the register one and the
+# TMA-staged persistent one (rank 48/49 default); both must give the oracle's
+# bits.  (2052, 64, 4100) gives ragged 256-position tiles and several tiles a
+# CTA, so the staged pipeline wraps its stages.
+RECONSTRUCT_VARIANTS = ["staged", "register"]
+
+
+@pytest.mark.parametrize("variant", RECONSTRUCT_VARIANTS)
 @pytest.mark.parametrize("name", list(PLANS))
-@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("shape", SHAPES + [(2052, 64, 4100)], ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("with_bias", [False, True])
-def test_reconstruct_matches_oracle_bitwise(name, shape, with_bias):
+def test_reconstruct_matches_oracle_bitwise(name, shape, with_bias, variant, monkeypatch):
+    monkeypatch.setenv("FMM_RECONSTRUCT_VARIANT", variant)
     M, K, N = shape
     _, _, bias = make_linear_inputs(M, K, N, seed=0, bias=True)
     s, _, _, P = _planes(PLANS[name], M, K, N)
@@ -106,10 +115,12 @@ def test_reconstruct_matches_oracle_bitwise(name, shape, with_bias):
     np.testing.assert_array_equal(_bits(C), oracle.bf16_bits(ref).view(np.int16))
 
 
+@pytest.mark.parametrize("variant", RECONSTRUCT_VARIANTS)
 @pytest.mark.parametrize("name", list(PLANS))
-def test_reconstruct_unaligned_bias_matches_aligned(name):
+def test_reconstruct_unaligned_bias_matches_aligned(name, variant, monkeypatch):
     """Bias vector loads (aligned bias) and element loads (offset bias) add the
     same values: identical bits."""
+    monkeypatch.setenv("FMM_RECONSTRUCT_VARIANT", variant)
     M, K, N = 130, 64, 2064
     _, _, bias = make_linear_inputs(M, K, N, seed=0, bias=True)
     s, _, _, P = _planes(PLANS[name], M, K, N)
