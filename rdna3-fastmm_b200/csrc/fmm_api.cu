@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -486,23 +487,28 @@ using PairCfg128 = LeafGemmPairConfig<128, 8>;
 
 enum GemmVariant { kVariantSingle = 0, kVariantPair256 = 1, kVariantPair128 = 2, kVariantPair192 = 3 };
 
-// Estimated relative cost of a variant: whole waves of tiles over the SMs (or
-// SM pairs), times the padded work one SM does per tile, divided by the
-// variant's measured throughput relative to the 1-SM 128x256 tile on B200
-// leaf shapes (a pair stages half of B per SM; 256x192 pairs measured 0.90 -
-// 0.97 of one SM, 256x128 pairs slower still and only used when forced).
+// Estimated relative cost of a variant: whole waves of full-tile equivalents
+// over the SMs (or SM pairs), times the padded work one SM does per tile,
+// divided by the variant's measured throughput relative to the 1-SM 128x256
+// tile on B200 leaf shapes (a pair stages half of B per SM; 256x192 pairs
+// measured 0.90 - 0.97 of one SM, 256x128 pairs slower still and only used
+// when forced).  The ragged last N tile counts only the columns its MMA
+// computes (the remainder rounded up to 16, or 32 for a pair).
 double variant_cost(int variant, int64_t rank, int64_t bm, int64_t bn, int sms) {
   const bool pair = variant != kVariantSingle;
   const int64_t tm = pair ? 256 : 128;
   const int64_t tn = variant == kVariantPair128 ? 128 : (variant == kVariantPair192 ? 192 : 256);
+  const int64_t granule = pair ? 32 : 16;
   const int64_t units = pair ? sms / 2 : sms;
   const double efficiency = variant == kVariantSingle    ? 1.0
                             : variant == kVariantPair256 ? 1.15
                             : variant == kVariantPair192 ? 0.95
                                                          : 0.70;
-  const int64_t tiles = rank * ceil_div(bm, tm) * ceil_div(bn, tn);
-  const int64_t waves = ceil_div(tiles, units);
-  return double(waves) * double(tm * tn / (pair ? 2 : 1)) / efficiency;
+  const int64_t full_n = bn / tn;
+  const int64_t last_cols = round_up(bn - full_n * tn, granule);
+  const double n_tiles = double(full_n) + double(last_cols) / double(tn);
+  const double waves = std::ceil(double(rank * ceil_div(bm, tm)) * n_tiles / double(units));
+  return waves * double(tm * tn / (pair ? 2 : 1)) / efficiency;
 }
 
 int choose_variant(int64_t rank, int64_t bm, int64_t bn, int sms) {
@@ -538,9 +544,11 @@ int ensure_smem_attribute(bool& done, Kernel kernel, size_t bytes) {
 template <class Cfg>
 int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_t ldk, int sms,
                 bool& configured, cudaStream_t stream) {
-  CUtensorMap map_l, map_r;
+  CUtensorMap map_l, map_r, map_r16;
   if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM)) return rc;
   if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, Cfg::kBN / 2)) return rc;
+  // 16-row boxes for the ragged last N tile's halves
+  if (int rc = plane_map(&map_r16, Rt, prm.bk, prm.bn, ldk, prm.rank, 16)) return rc;
   {
     std::lock_guard<std::mutex> lock(g_device_mutex);
     if (int rc = ensure_smem_attribute(configured, leaf_gemm_pair_kernel<Cfg>, Cfg::kSmemBytes)) return rc;
@@ -559,7 +567,7 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg>, map_l, map_r, prm);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg>, map_l, map_r, map_r16, prm);
   if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM (pair) launch");
   return FMM_OK;
 }

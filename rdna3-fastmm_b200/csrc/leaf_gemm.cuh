@@ -66,6 +66,16 @@ __device__ __forceinline__ void leaf_tile_coords(const LeafGemmParams& p, int t,
   tn = in_group / group_rows;
 }
 
+// Columns the MMA computes for N tile tn: the whole tile, or for the ragged
+// last tile the remainder rounded up to `granule` (a valid MMA N for the
+// instruction shape), so no tensor-core time goes to columns past bn.  Every
+// column the epilogue stores (below ldp = bn rounded up to 8) lies inside it.
+__device__ __forceinline__ int tile_n_columns(const LeafGemmParams& p, int tn, int tile_n, int granule) {
+  const int64_t rem = p.bn - static_cast<int64_t>(tn) * tile_n;
+  if (rem >= tile_n) return tile_n;
+  return static_cast<int>((rem + granule - 1) / granule * granule);
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     leaf_gemm_kernel(const __grid_constant__ CUtensorMap tmap_l,
@@ -163,7 +173,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(kGemmBM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -171,6 +180,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       bool issued_any = false;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        int r, tm, tn;
+        leaf_tile_coords(p, t, r, tm, tn);
+        // M = 128, cta_group::1: N a multiple of 16
+        const uint32_t idesc = idesc_f16_f32(kGemmBM, static_cast<uint32_t>(tile_n_columns(p, tn, BN, 16)));
         if (!mbar_wait_bounded(tempty_bar + 8 * acc, acc_phase ^ 1u, abort, p.timeout_ns, 2)) {
           ok = false;
           break;
@@ -231,8 +244,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __half* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
       const uint32_t t_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int n_cols = tile_n_columns(p, tn, BN, 16);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < n_cols; c += 32) {
         uint32_t v[32];
         tc_ld_32x32b_x32(t_addr + c, v);
         tc_wait_ld();
@@ -308,7 +322,8 @@ struct LeafGemmPairConfig {
 template <class Cfg>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     leaf_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_l,
-                          const __grid_constant__ CUtensorMap tmap_r, const LeafGemmParams p) {
+                          const __grid_constant__ CUtensorMap tmap_r,
+                          const __grid_constant__ CUtensorMap tmap_r16, const LeafGemmParams p) {
   constexpr int BN = Cfg::kBN;
   constexpr int STAGES = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -346,6 +361,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmap_l);
     prefetch_tmap(&tmap_r);
+    prefetch_tmap(&tmap_r16);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -375,16 +391,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int r, tm, tn;
         leaf_tile_coords(q, t, r, tm, tn);
         const int a_row = tm * Cfg::kTileM + static_cast<int>(cta) * kGemmBM;
-        const int b_row = tn * BN + static_cast<int>(cta) * (BN / 2);
+        // Each CTA supplies half of the N columns the pair's MMA computes.  A
+        // ragged last tile loads exactly its half in 16-row boxes: a BN/2-row
+        // box would fetch rows that belong to the other CTA's half.
+        const int n_cols = tile_n_columns(q, tn, BN, 32);
+        const int half = n_cols / 2;
+        const int b_row = tn * BN + static_cast<int>(cta) * half;
+        const uint32_t stage_tx = 2u * (Cfg::kABytes + static_cast<uint32_t>(half) * kGemmBK * 2u);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait_bounded_cluster(empty_bar + 8 * stage, phase ^ 1u, abort, p.timeout_ns, 11)) {
             ok = false;
             break;
           }
           const uint32_t full_even = map_to_cta(full_bar + 8 * stage, 0);
-          if (cta == 0) mbar_arrive_expect_tx(full_bar + 8 * stage, 2 * Cfg::kStageBytes);
+          if (cta == 0) mbar_arrive_expect_tx(full_bar + 8 * stage, stage_tx);
           tma_load_3d_pair(a_base + stage * Cfg::kABytes, &tmap_l, full_even, kb * kGemmBK, a_row, r);
-          tma_load_3d_pair(b_base + stage * Cfg::kBBytes, &tmap_r, full_even, kb * kGemmBK, b_row, r);
+          if (n_cols == BN) {
+            tma_load_3d_pair(b_base + stage * Cfg::kBBytes, &tmap_r, full_even, kb * kGemmBK, b_row, r);
+          } else {
+            for (int j = 0; j < half; j += 16)
+              tma_load_3d_pair(b_base + stage * Cfg::kBBytes + static_cast<uint32_t>(j) * kGemmBK * 2u,
+                               &tmap_r16, full_even, kb * kGemmBK, b_row + j, r);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -404,7 +432,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
     if (cta == 0 && lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(Cfg::kTileM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -412,6 +439,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       bool issued_any = false;
       for (int t = pair; t < total_tiles && ok; t += pairs) {
+        int r, tm, tn;
+        leaf_tile_coords(q, t, r, tm, tn);
+        // M = 256, cta_group::2: N a multiple of 32 (16 columns from each CTA)
+        const uint32_t idesc =
+            idesc_f16_f32(Cfg::kTileM, static_cast<uint32_t>(tile_n_columns(q, tn, BN, 32)));
         if (!mbar_wait_bounded_cluster(tempty_bar + 8 * acc, acc_phase ^ 1u, abort, p.timeout_ns, 12)) {
           ok = false;
           break;
@@ -472,8 +504,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __half* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
       const uint32_t t_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int n_cols = tile_n_columns(q, tn, BN, 32);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < n_cols; c += 32) {
         uint32_t v[32];
         tc_ld_32x32b_x32(t_addr + c, v);
         tc_wait_ld();
