@@ -62,7 +62,7 @@ OPERATOR_NAMES = {"rank7": "rdna3_fastmm::linear_rank7", "rank49": "rdna3_fastmm
                   "rank48": "rdna3_fastmm::linear_rank48", "rank343": "(none)"}
 DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16}
 ENVIRONMENT_KEYS = ("CUDA_VISIBLE_DEVICES", "CUBLAS_WORKSPACE_CONFIG", "NCCL_DEBUG",
-                    "FMM_LEAF_GEMM_VARIANT", "PYTORCH_CUDA_ALLOC_CONF")
+                    "FMM_LEAF_GEMM_VARIANT", "FMM_RECONSTRUCT_VARIANT", "PYTORCH_CUDA_ALLOC_CONF")
 
 
 @dataclass(frozen=True)
