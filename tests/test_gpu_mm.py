@@ -43,8 +43,10 @@ def test_right_kn_transform_matches_oracle_bitwise(name, dtype, shape):
     assert torch.all(Rt[:, :, bk:] == 0)
 
 
+@pytest.mark.parametrize("variant", ["staged", "register"])
 @pytest.mark.parametrize("name", ["rank7", "rank49"])
-def test_fp16_left_transform_and_fp16_reconstruct_match_oracle(name):
+def test_fp16_left_transform_and_fp16_reconstruct_match_oracle(name, variant, monkeypatch):
+    monkeypatch.setenv("FMM_RECONSTRUCT_VARIANT", variant)  # rank 49: TMA-staged or register kernel
     M, K, N = 257, 263, 269
     A, _, bias = make_linear_inputs(M, K, N, seed=6, bias=True)
     A, bias = A.to(torch.float16), bias.to(torch.float16)
