@@ -315,7 +315,9 @@ __device__ __forceinline__ void recombine_vector(const typename VecIO<VEC>::H (&
 }
 
 // Unfused reconstruct: P[r][bm][ldp] FP16 -> C[M,N].  All R product vectors
-// are loaded before the arithmetic, as in the input side.
+// are loaded before the arithmetic, as in the input side.  The rank-7
+// reconstruct; rank 48/49 use the TMA-staged form (reconstruct_staged.cuh)
+// unless FMM_RECONSTRUCT_VARIANT=register.
 template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
     const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
