@@ -1,0 +1,125 @@
+"""Parity at the benchmark configurations' full sizes.
+
+The CPU oracle cannot run a whole 8192^3 linear in seconds, but every stage
+of the path is position-wise, so sampled positions pin the full-size launch:
+
+* row block ``i`` of the left planes depends only on rows ``p_r * bm + i`` of
+  ``A`` (one per block row ``p_r``): the oracle's left transform of that
+  ``s``-row matrix must give ``L[:, i, :]`` bit for bit;
+* likewise column block ``j`` of the weight planes and rows
+  ``p_c * bn + j`` of ``W``;
+* row ``i`` of the products and the output rows ``p_r * bm + i`` for the
+  output transform (bit for bit, with the bias);
+* the leaf GEMM's sampled rows against an FP64 product of the same planes
+  within one FP16 ulp plus the FP32 accumulation bound;
+* the whole call through the plan API, dynamic and prepacked, equals the
+  staged launches bit for bit.
+
+Sampled block rows always include the first and the last (padded) one.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from inputs import f32, make_linear_inputs
+from oracle import fmm_oracle as oracle
+from rdna3_fastmm import _native
+from rdna3_fastmm.runtime import MatrixShape, Rank7Plan, Rank48Plan, Rank49Plan
+
+pytestmark = pytest.mark.gpu
+
+PLANS = {"rank7": Rank7Plan, "rank48": Rank48Plan, "rank49": Rank49Plan}
+# (scheme, M, K, N, bias): the benchmark configurations c2, c3, c4, c5a, c5b
+CONFIGS = {
+    "c2": ("rank7", 4096, 4096, 12288, False),
+    "c3": ("rank7", 4992, 16384, 4096, True),
+    "c4": ("rank49", 8214, 12288, 4608, False),
+    "c5a": ("rank48", 8192, 8192, 8192, False),
+    "c5b": ("rank48", 65536, 4608, 12288, False),
+}
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).cpu().numpy()
+
+
+def _sample(n: int, count: int, seed: int) -> list[int]:
+    rng = np.random.default_rng(seed)
+    picked = set(rng.choice(n, size=min(count, n), replace=False).tolist()) | {0, n - 1}
+    return sorted(picked)
+
+
+def _block_rows(X: torch.Tensor, s: int, pitch: int, index: int) -> torch.Tensor:
+    """Rows ``p * pitch + index`` of X for p < s; missing rows (past the end)
+    are zero, which is the zero padding of the last block."""
+    out = torch.zeros((s, X.shape[1]), dtype=X.dtype)
+    for p in range(s):
+        row = p * pitch + index
+        if row < X.shape[0]:
+            out[p] = X[row]
+    return out
+
+
+@pytest.mark.parametrize("config", list(CONFIGS))
+def test_full_size_stages_match_oracle_on_sampled_positions(config):
+    name, M, K, N, with_bias = CONFIGS[config]
+    plan_type = PLANS[name]
+    s_ = plan_type.scheme_size
+    A, W, bias = make_linear_inputs(M, K, N, seed=0, bias=with_bias)
+    shape = MatrixShape.from_dimensions(M, K, N, s_)
+    bm, bk, bn = shape.block_rows, shape.block_inner, shape.block_columns
+    R = plan_type.rank
+    dev = torch.device("cuda")
+    Ad, Wd = A.to(dev), W.to(dev)
+    bd = bias.to(dev) if with_bias else None
+    L = torch.empty((R, bm, shape.inner_pitch), device=dev, dtype=torch.float16)
+    Rt = torch.empty((R, bn, shape.inner_pitch), device=dev, dtype=torch.float16)
+    P = torch.empty((R, bm, shape.column_pitch), device=dev, dtype=torch.float16)
+    C = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+    _native.transform_a(name, Ad, L)
+    _native.transform_w(name, Wd, Rt)
+    _native.leaf_gemm(R, L, Rt, bm, bn, bk, P)
+    _native.reconstruct(name, P, M, N, bd, C)
+    torch.cuda.synchronize()
+
+    # left and weight transforms, bit for bit
+    for i in _sample(bm, 6, seed=1):
+        ref = oracle.left_transform(name, f32(_block_rows(A, s_, bm, i)))  # [R, 1, bk]
+        np.testing.assert_array_equal(_bits(L[:, i, :bk]), ref[:, 0, :].view(np.int16))
+    for j in _sample(bn, 6, seed=2):
+        ref = oracle.weight_transform(name, f32(_block_rows(W, s_, bn, j)))  # [R, bk, 1]
+        np.testing.assert_array_equal(_bits(Rt[:, j, :bk]), ref[:, :, 0].view(np.int16))
+
+    # leaf products within the FP16 rounding + FP32 accumulation bound
+    # (FP64 on the device: IEEE double products of the same FP16 planes)
+    Rt64 = Rt[:, :, :bk].double()
+    for i in _sample(bm, 4, seed=3):
+        a = L[:, i, :bk].double()  # [R, bk]
+        exact = torch.einsum("rk,rnk->rn", a, Rt64)
+        magnitude = torch.einsum("rk,rnk->rn", a.abs(), Rt64.abs())
+        got = P[:, i, :bn].double()
+        ulp = torch.clamp(exact.abs(), min=2.0**-14) * 2.0**-10
+        assert torch.all((got - exact).abs() <= ulp + (bk + 2) * 2.0**-23 * magnitude)
+    del Rt64
+
+    # output transform of the GPU's own products, bit for bit, bias included
+    for i in _sample(bm, 6, seed=4):
+        rows = [p * bm + i for p in range(s_) if p * bm + i < M]
+        products = P[:, i:i + 1, :bn].cpu().numpy()
+        ref = oracle.output_transform(name, products, len(rows), N, f32(bias) if with_bias else None)
+        np.testing.assert_array_equal(_bits(C[rows]), oracle.bf16_bits(ref).view(np.int16))
+    assert torch.isfinite(C.float()).all()
+
+    # the plan API (dynamic: paired input transforms; prepacked: packed weight)
+    # gives the same bits as the staged launches
+    plan = plan_type(M, K, N, dev, dtype=torch.bfloat16, compute_dtype=torch.float16)
+    del L, Rt, P
+    ws = plan.allocate_workspace(max_free_memory_fraction=0.9)
+    dynamic = plan.run_linear(Ad, Wd, ws, bd)
+    assert torch.equal(dynamic.view(torch.int16), C.view(torch.int16))
+    del ws, dynamic
+    packed = plan.pack_weight(Wd, 0.9)
+    ws = plan.allocate_workspace(max_free_memory_fraction=0.9, prepacked_right=True)
+    prepacked = plan.run_linear_packed(Ad, packed, ws, bd)
+    assert torch.equal(prepacked.view(torch.int16), C.view(torch.int16))
