@@ -13,7 +13,9 @@ the line carries per-kernel-class times and roofline fractions; L2 is flushed
 every rank runs the whole workload on its own GPU; the path has no exchange
 step).  ``e2e`` is the same metric through the public plan API with pinned
 host buffers, host->device copies of A and the weight and the device->host
-copy of C inside the timed region.  ``cpu_baseline`` is the CPU oracle on a
+copy of C inside the timed region; consecutive steps alternate over two
+streams with their own buffers, so one step's input copies overlap the
+previous step's compute and result copy.  ``cpu_baseline`` is the CPU oracle on a
 bounded row sample of the same workload.  ``--impl reference`` times that CPU
 implementation alone (the reference is a ROCm/Triton project with no B200
 path; its algorithm's CPU restatement is the reference arm).
@@ -324,44 +326,64 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     torch.cuda.synchronize(device)
     cublas_ms = statistics.median(a.elapsed_time(b) for a, b in cub)
 
-    # end to end through the public plan API with pinned host buffers
+    # End to end through the public plan API with pinned host buffers.  Steps
+    # alternate over `lanes` streams, each with its own device inputs,
+    # workspace, output and pinned result buffer, so the host->device copies of
+    # step k+1 run while step k computes and copies its result back (PCIe is
+    # full duplex); every step still copies all of its inputs in and its whole
+    # result out inside the timed region.
     A_pin, W_pin = A_h.pin_memory(), W_h.pin_memory()
     b_pin = b_h.pin_memory() if b_h is not None else None
-    C_pin = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-    A_d, W_d = torch.empty_like(A), torch.empty_like(W)
-    b_d = torch.empty_like(bias) if bias is not None else None
-
-    if shard:
-        C_pin = torch.empty((layer.rows if gathered is None else gathered.shape[0], N),
-                            dtype=torch.bfloat16).pin_memory()
-
-    def e2e_step():
-        A_d.copy_(A_pin, non_blocking=True)
-        if not prepacked:
-            W_d.copy_(W_pin, non_blocking=True)
-        if b_d is not None:
-            b_d.copy_(b_pin, non_blocking=True)
+    lanes = 1 if shard else max(1, args.e2e_lanes)
+    lane_state = []
+    for k in range(lanes):
+        lane = {"stream": stream if lanes == 1 else torch.cuda.Stream(device=device),
+                "A": torch.empty_like(A), "W": torch.empty_like(W),
+                "b": torch.empty_like(bias) if bias is not None else None}
         if shard:
-            res = layer(A_d, out=gathered)
-        elif prepacked:
-            res = plan.run_linear_packed(A_d, packed, ws, b_d, out)
+            lane["C_pin"] = torch.empty((layer.rows if gathered is None else gathered.shape[0], N),
+                                        dtype=torch.bfloat16).pin_memory()
         else:
-            res = plan.run_linear(A_d, W_d, ws, b_d, out)
-        C_pin.copy_(res, non_blocking=True)
+            lane["ws"] = ws if k == 0 else plan.allocate_workspace(0.9, prepacked_right=prepacked)
+            lane["out"] = out if k == 0 else torch.empty_like(out)
+            lane["C_pin"] = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+        lane_state.append(lane)
+
+    def e2e_step(lane):
+        with torch.cuda.stream(lane["stream"]):
+            A_d, W_d, b_d = lane["A"], lane["W"], lane["b"]
+            A_d.copy_(A_pin, non_blocking=True)
+            if not prepacked:
+                W_d.copy_(W_pin, non_blocking=True)
+            if b_d is not None:
+                b_d.copy_(b_pin, non_blocking=True)
+            if shard:
+                res = layer(A_d, out=gathered)
+            elif prepacked:
+                res = plan.run_linear_packed(A_d, packed, lane["ws"], b_d, lane["out"])
+            else:
+                res = plan.run_linear(A_d, W_d, lane["ws"], b_d, lane["out"])
+            lane["C_pin"].copy_(res, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(2):
-        e2e_step()
+    e2e_steps += (-e2e_steps) % lanes
+    for k in range(2 * lanes):
+        e2e_step(lane_state[k % lanes])
     torch.cuda.synchronize(device)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    for lane in lane_state:
+        lane["stream"].wait_event(e0)
+    for k in range(e2e_steps):
+        e2e_step(lane_state[k % lanes])
+    for lane in lane_state:
+        stream.wait_stream(lane["stream"])
     e1.record(stream)
     torch.cuda.synchronize(device)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    C_pin = lane_state[0]["C_pin"]
     h2d = A_h.numel() * 2 + (0 if prepacked else W_h.numel() * 2) + (N * 2 if b_h is not None else 0)
     d2h = C_pin.numel() * 2
 
@@ -449,7 +471,8 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         "e2e": {"value": round(job_flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": ("RowShardedLinear (gather)" if shard else
-                f"{type(plan).__name__}.run_linear{'_packed' if prepacked else ''}")},
+                f"{type(plan).__name__}.run_linear{'_packed' if prepacked else ''}"),
+                "streams": lanes},
         "clocks": clocks.summary(),
         "gpu_launches": args.steps * 3,
     }
@@ -481,6 +504,10 @@ def main() -> None:
                         help="override M (smaller cases for profiler captures)")
     parser.add_argument("--shard", action="store_true",
                         help="split M over the ranks and all-gather C (strong scaling)")
+    parser.add_argument("--e2e-lanes", type=int, default=2,
+                        help="streams the e2e steps alternate over, each with its own buffers, so "
+                             "one step's host->device copies overlap the previous step's compute "
+                             "and device->host copy (1: strictly one step after another)")
     parser.add_argument("--chunks", type=int, default=None,
                         help="row chunks per rank in --shard mode (default: 4 with the NCCL gather, "
                              "which overlaps the next chunk; 1 with --transport p2p, whose gathering "
