@@ -303,20 +303,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //            thread issues the MMAs and the multicast commits.
 //   warps 2-5 epilogue: each CTA drains its own 128 accumulator lanes and
 //            signals the even CTA's `tmem_empty` barrier (8 arrivals).
-// No TMA multicast is used: every CTA loads only its own halves.
-template <int BN, int STAGES>
+// No TMA multicast is used: every CTA loads only its own halves.  Deep leaves
+// (bk >= 3072) use 128-deep k-blocks in 3 stages: two 64-deep atom columns per
+// operand and stage, half the barrier round trips per FLOP.
+template <int BN, int STAGES, int BK = kGemmBK>
 struct LeafGemmPairConfig {
   static constexpr int kBN = BN;
   static constexpr int kStages = STAGES;
-  static constexpr int kTileM = 2 * kGemmBM;                  // 256 rows per pair
-  static constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;   // this CTA's L half: 16 KiB
-  static constexpr uint32_t kBBytes = (BN / 2) * kGemmBK * 2;  // this CTA's Rt half
+  // k-block depth 64 or 128: one or two 64-deep columns of 128-byte swizzle
+  // atoms per operand and stage
+  static constexpr int kBK = BK;
+  static constexpr int kAtomK = 64;  // k per swizzle-atom column (128-byte rows)
+  static constexpr int kAtoms = BK / kAtomK;
+  static constexpr uint32_t kAAtomBytes = kGemmBM * kAtomK * 2;
+  static constexpr uint32_t kBAtomBytes = (BN / 2) * kAtomK * 2;
+  static constexpr int kTileM = 2 * kGemmBM;              // 256 rows per pair
+  static constexpr uint32_t kABytes = kGemmBM * BK * 2;   // this CTA's L half: 16 KiB at BK=64
+  static constexpr uint32_t kBBytes = (BN / 2) * BK * 2;  // this CTA's Rt half
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   // two accumulators of BN columns; the allocation is a power of two
   static constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256 : 512;
-  static constexpr size_t kSmemBytes = size_t(STAGES) * kStageBytes + 1024 + 256;
+  // stages + 1 KiB slack for the 1024-byte alignment + the barrier block
+  // (2 * STAGES + 5 barriers, the TMEM slot and the abort flag)
+  static constexpr size_t kSmemBytes = size_t(STAGES) * kStageBytes + 1024 + 8 * (2 * STAGES + 8);
   static_assert(2 * BN <= 512 && BN % 32 == 0, "two BN-column accumulators must fit in TMEM");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+  static_assert(BK == 64 || BK == 128, "k-block depth");
 };
 
 template <class Cfg>
@@ -326,6 +338,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                           const __grid_constant__ CUtensorMap tmap_r16, const LeafGemmParams p) {
   constexpr int BN = Cfg::kBN;
   constexpr int STAGES = Cfg::kStages;
+  constexpr int BK = Cfg::kBK;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -378,7 +391,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   q.tiles_m = tiles_m;
   q.tiles_n = tiles_n;
   const int total_tiles = p.rank * tiles_m * tiles_n;
-  const int k_blocks = static_cast<int>((p.bk + kGemmBK - 1) / kGemmBK);
+  const int k_blocks = static_cast<int>((p.bk + BK - 1) / BK);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producers
@@ -397,7 +410,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int n_cols = tile_n_columns(q, tn, BN, 32);
         const int half = n_cols / 2;
         const int b_row = tn * BN + static_cast<int>(cta) * half;
-        const uint32_t stage_tx = 2u * (Cfg::kABytes + static_cast<uint32_t>(half) * kGemmBK * 2u);
+        const uint32_t stage_tx = 2u * (Cfg::kABytes + static_cast<uint32_t>(half) * BK * 2u);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait_bounded_cluster(empty_bar + 8 * stage, phase ^ 1u, abort, p.timeout_ns, 11)) {
             ok = false;
@@ -405,13 +418,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           const uint32_t full_even = map_to_cta(full_bar + 8 * stage, 0);
           if (cta == 0) mbar_arrive_expect_tx(full_bar + 8 * stage, stage_tx);
-          tma_load_3d_pair(a_base + stage * Cfg::kABytes, &tmap_l, full_even, kb * kGemmBK, a_row, r);
-          if (n_cols == BN) {
-            tma_load_3d_pair(b_base + stage * Cfg::kBBytes, &tmap_r, full_even, kb * kGemmBK, b_row, r);
-          } else {
-            for (int j = 0; j < half; j += 16)
-              tma_load_3d_pair(b_base + stage * Cfg::kBBytes + static_cast<uint32_t>(j) * kGemmBK * 2u,
-                               &tmap_r16, full_even, kb * kGemmBK, b_row + j, r);
+#pragma unroll
+          for (int at = 0; at < Cfg::kAtoms; ++at) {
+            const int k0 = kb * BK + at * Cfg::kAtomK;
+            tma_load_3d_pair(a_base + stage * Cfg::kABytes + at * Cfg::kAAtomBytes, &tmap_l, full_even,
+                             k0, a_row, r);
+            const uint32_t b_dst = b_base + stage * Cfg::kBBytes + at * Cfg::kBAtomBytes;
+            if (n_cols == BN) {
+              tma_load_3d_pair(b_dst, &tmap_r, full_even, k0, b_row, r);
+            } else {
+              for (int j = 0; j < half; j += 16)
+                tma_load_3d_pair(b_dst + static_cast<uint32_t>(j) * Cfg::kAtomK * 2u, &tmap_r16, full_even,
+                                 k0, b_row + j, r);
+            }
           }
           ++issued;
           if (++stage == STAGES) {
@@ -459,9 +478,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t a_addr = a_base + stage * Cfg::kABytes;
           const uint32_t b_addr = b_base + stage * Cfg::kBBytes;
 #pragma unroll
-          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
-            tc_mma_f16_pair(d_tmem, smem_desc_k_sw128(a_addr + kk * 32),
-                            smem_desc_k_sw128(b_addr + kk * 32), idesc,
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // 16-deep step kk: atom column kk / (kAtomK / 16), 32 bytes per step inside it
+            constexpr int kSteps = Cfg::kAtomK / 16;
+            const uint32_t a_off = (kk / kSteps) * Cfg::kAAtomBytes + (kk % kSteps) * 32;
+            const uint32_t b_off = (kk / kSteps) * Cfg::kBAtomBytes + (kk % kSteps) * 32;
+            tc_mma_f16_pair(d_tmem, smem_desc_k_sw128(a_addr + a_off),
+                            smem_desc_k_sw128(b_addr + b_off), idesc,
                             (kb > 0 || kk > 0) ? 1u : 0u);
           }
           issued_any = true;

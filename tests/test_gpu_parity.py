@@ -139,14 +139,15 @@ def test_reconstruct_unaligned_bias_matches_aligned(name, variant, monkeypatch):
     np.testing.assert_array_equal(_bits(C1), oracle.bf16_bits(ref).view(np.int16))
 
 
-@pytest.mark.parametrize("variant", ["single", "pair256", "pair192", "pair128"])
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair192", "pair128", "pair256k128"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
     [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (2, 129, 257, 1000), (48, 64, 72, 130),
      (5, 700, 900, 520)],
 )
 def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch):
-    """Every leaf-GEMM kernel (1-SM 128x256, 2-SM 256x256, 2-SM 256x128)."""
+    """Every leaf-GEMM kernel (1-SM 128x256; 2-SM 256x256, 256x192, 256x128 with 64-deep
+    k-blocks; 2-SM 256x256 with 128-deep k-blocks)."""
     monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
     g = torch.Generator().manual_seed(rank * 1000 + bm)
     ldk = -(-bk // 8) * 8
