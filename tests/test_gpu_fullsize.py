@@ -15,17 +15,20 @@ of the path is position-wise, so sampled positions pin the full-size launch:
 * the whole call through the plan API, dynamic and prepacked, equals the
   staged launches bit for bit.
 
-Sampled block rows always include the first and the last (padded) one.
+Sampled block rows always include the first and the last (padded) one.  The
+rank-343 FP16 square product is checked the same way at 16384^3, its
+tensor-core reconstruct within one FP16 ulp plus the FP32 accumulation bound
+of the 343-term sum.
 """
 
 import numpy as np
 import pytest
 import torch
 
-from inputs import f32, make_linear_inputs
+from inputs import f32, make_linear_inputs, randn_fp16
 from oracle import fmm_oracle as oracle
 from rdna3_fastmm import _native
-from rdna3_fastmm.runtime import MatrixShape, Rank7Plan, Rank48Plan, Rank49Plan
+from rdna3_fastmm.runtime import MatrixShape, Rank7Plan, Rank48Plan, Rank49Plan, Rank343Plan
 
 pytestmark = pytest.mark.gpu
 
@@ -123,3 +126,73 @@ def test_full_size_stages_match_oracle_on_sampled_positions(config):
     ws = plan.allocate_workspace(max_free_memory_fraction=0.9, prepacked_right=True)
     prepacked = plan.run_linear_packed(Ad, packed, ws, bd)
     assert torch.equal(prepacked.view(torch.int16), C.view(torch.int16))
+
+
+def _leaf_rows_within_bound(L, Rt, P, rows, bk, bn):
+    """Sampled product rows against a device-FP64 product of the same planes."""
+    Rt64 = Rt[:, :, :bk].double()
+    for i in rows:
+        a = L[:, i, :bk].double()
+        exact = torch.einsum("rk,rnk->rn", a, Rt64)
+        magnitude = torch.einsum("rk,rnk->rn", a.abs(), Rt64.abs())
+        got = P[:, i, :bn].double()
+        ulp = torch.clamp(exact.abs(), min=2.0**-14) * 2.0**-10
+        assert torch.all((got - exact).abs() <= ulp + (bk + 2) * 2.0**-23 * magnitude)
+
+
+def test_rank343_full_size_stages_match_oracle_on_sampled_positions():
+    """Rank-343 FP16 square product at 16384^3 (the plain-mm API: ``B[K, N]``
+    through the K x N right transform), the same sampled checks; the
+    tensor-core reconstruct is held to one FP16 ulp of the oracle's
+    ascending-order sum."""
+    M = K = N = 16384
+    s_ = 8
+    A, B = randn_fp16((M, K), 0), randn_fp16((K, N), 1)
+    shape = MatrixShape.from_dimensions(M, K, N, s_)
+    bm, bk, bn = shape.block_rows, shape.block_inner, shape.block_columns
+    dev = torch.device("cuda")
+    Ad, Bd = A.to(dev), B.to(dev)
+    L = torch.empty((343, bm, shape.inner_pitch), device=dev, dtype=torch.float16)
+    Rt = torch.empty((343, bn, shape.inner_pitch), device=dev, dtype=torch.float16)
+    P = torch.empty((343, bm, shape.column_pitch), device=dev, dtype=torch.float16)
+    C = torch.empty((M, N), device=dev, dtype=torch.float16)
+    _native.transform_a("rank343", Ad, L)
+    _native.transform_b("rank343", Bd, Rt)
+    _native.leaf_gemm(343, L, Rt, bm, bn, bk, P)
+    _native.reconstruct("rank343", P, M, N, None, C)
+    torch.cuda.synchronize()
+
+    for i in _sample(bm, 4, seed=1):
+        ref = oracle.left_transform("rank343", f32(_block_rows(A, s_, bm, i)))
+        np.testing.assert_array_equal(_bits(L[:, i, :bk]), ref[:, 0, :].view(np.int16))
+    for j in _sample(bn, 4, seed=2):
+        cols = [p * bn + j for p in range(s_)]
+        ref = oracle.right_transform("rank343", f32(B[:, cols]))  # [343, bk, 1]
+        np.testing.assert_array_equal(_bits(Rt[:, j, :bk]), ref[:, :, 0].view(np.int16))
+
+    _leaf_rows_within_bound(L, Rt, P, _sample(bm, 2, seed=3), bk, bn)
+
+    # |C_o - ref| <= one FP16 ulp + the FP32 accumulation bound of the 343-term
+    # +-1 sum (the tensor core adds in its own order; where the sum cancels,
+    # that bound exceeds an ulp of the small result)
+    W = np.abs(oracle.output_coefficients("rank343")).astype(np.float64)  # [64, 343]
+    for i in _sample(bm, 4, seed=4):
+        rows = [p * bm + i for p in range(s_)]
+        products = P[:, i:i + 1, :bn].cpu().numpy()
+        ref = oracle.output_transform("rank343", products, s_, N, None, "fp16").astype(np.float16)
+        magnitude = (W @ np.abs(products[:, 0, :].astype(np.float64)))  # [64, bn], output o = (br, bc)
+        bound_mag = magnitude.reshape(s_, s_, bn).reshape(s_, s_ * bn)  # row br, column bc * bn + c
+        got = C[rows].cpu().numpy()
+        ulp = np.spacing(np.abs(ref)).astype(np.float64)
+        err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+        assert np.all(err <= ulp + 345 * 2.0**-24 * bound_mag)
+        assert np.mean(got == ref) > 0.99
+    assert torch.isfinite(C).all()
+
+    plan = Rank343Plan(M, K, N, dev)
+    del L, Rt, P
+    dynamic = plan.run(Ad, Bd, plan.allocate_workspace(0.9))
+    assert torch.equal(dynamic.view(torch.int16), C.view(torch.int16))
+    del dynamic
+    packed = plan.run_packed(Ad, plan.pack_right(Bd, 0.9), plan.allocate_workspace(0.9, prepacked_right=True))
+    assert torch.equal(packed.view(torch.int16), C.view(torch.int16))
