@@ -12,7 +12,9 @@ run on CPU tensors under ``TRITON_INTERPRET=1`` with FP16 operands, as
 ``Rank7Plan.run`` / ``Rank49Plan.run`` launch them (``runtime.py:597-698``):
 ``left_transform_kernel`` on ``A[M, K]``, ``right_transform_kernel`` on the
 contiguous ``B[K, N]`` and ``output_transform_kernel`` into an FP16 ``C``
-(FP32 -> FP16 stores are correctly rounded in the interpreter).
+(FP32 -> FP16 stores are correctly rounded in the interpreter); and, for the
+FP16 linear plans, ``right_transform_weight_kernel`` on the native
+``weight[N, K] = B^T`` and ``output_transform_bias_kernel`` with an FP16 bias.
 
 Writes ``golden_mm.json`` (SHA-256 digests) and ``golden_mm.npz`` (full
 arrays of the small cases).
@@ -67,19 +69,28 @@ def main() -> None:
             R = torch.empty((rank, bk, bn), dtype=torch.float16)
             module.right_transform_kernel[(triton.cdiv(bk * bn, BLOCK_ELEMENTS),)](
                 B, R, K, N, bk, bn, bk, bn, BLOCK_ELEMENTS)
+            W = B.t().contiguous()
+            Rw = torch.empty((rank, bk, bn), dtype=torch.float16)
+            module.right_transform_weight_kernel[(triton.cdiv(bk, 4), triton.cdiv(bn, 64))](
+                W, Rw, N, K, bk, bn, 4, 64)
             P = random_products(rank, bm, bn, seed=3)
+            bias = randn_fp16((N,), 2, 0.02)
+            grid = (triton.cdiv(bm * bn, BLOCK_ELEMENTS),)
             C = torch.zeros((M, N), dtype=torch.float16)
-            module.output_transform_kernel[(triton.cdiv(bm * bn, BLOCK_ELEMENTS),)](
-                P, C, bm, bn, M, N, bm, bn, BLOCK_ELEMENTS)
+            module.output_transform_kernel[grid](P, C, bm, bn, M, N, bm, bn, BLOCK_ELEMENTS)
+            Cb = torch.zeros((M, N), dtype=torch.float16)
+            module.output_transform_bias_kernel[grid](P, Cb, bias, bm, bn, M, N, bm, bn, BLOCK_ELEMENTS)
             record["cases"].append({
-                "scheme": name, "shape": [M, K, N], "seeds": {"A": 0, "B": 1, "P": 3},
-                "inputs": {"A": digest(A), "B": digest(B), "P": digest(P)},
-                "left": digest(L), "right": digest(R), "output": digest(C)})
+                "scheme": name, "shape": [M, K, N], "seeds": {"A": 0, "B": 1, "P": 3, "bias": 2},
+                "inputs": {"A": digest(A), "B": digest(B), "P": digest(P), "bias": digest(bias)},
+                "left": digest(L), "right": digest(R), "weight": digest(Rw), "output": digest(C),
+                "output_bias": digest(Cb)})
             if (M, K, N) in SMALL:
                 key = f"{name}_{M}x{K}x{N}"
                 arrays[key + "_left"] = L.view(torch.int16).numpy()
                 arrays[key + "_right"] = R.view(torch.int16).numpy()
                 arrays[key + "_output"] = C.view(torch.int16).numpy()
+                arrays[key + "_output_bias"] = Cb.view(torch.int16).numpy()
             print(name, (M, K, N), "done", flush=True)
     (HERE / "golden_mm.json").write_text(json.dumps(record, indent=1) + "\n")
     np.savez_compressed(HERE / "golden_mm.npz", **arrays)
