@@ -180,8 +180,9 @@ int fmm_linear(int scheme, int dtype, const void* A, const void* W, const void* 
  * calls on a device share the one array, so calls that overlap on the GPU
  * (on different streams, or from different threads) race; serialise them.
  * Nothing in the array has to start at zero: each call writes every plane
- * element it later reads.  No counterpart in the reference (its Python plans
- * always allocate through PyTorch). */
+ * element it later reads.  Schemes 7, 48 and 49 only (BF16 operands); any other
+ * scheme id returns FMM_ERR_UNSUPPORTED.  No counterpart in the reference (its
+ * Python plans always allocate through PyTorch). */
 int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bias, void* C,
                        int64_t M, int64_t K, int64_t N, fmm_stream_t stream);
 

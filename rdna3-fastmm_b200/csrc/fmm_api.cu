@@ -912,6 +912,10 @@ int fmm_linear(int scheme, int dtype, const void* A, const void* W, const void* 
 
 int fmm_linear_noalloc(int scheme, const void* A, const void* W, const void* bias, void* C,
                        int64_t M, int64_t K, int64_t N, fmm_stream_t stream) {
+  // BF16 linears only: rank 343 takes FP16 operands, so it has no BF16 form to run here
+  if (scheme != FMM_SCHEME_RANK7 && scheme != FMM_SCHEME_RANK48 && scheme != FMM_SCHEME_RANK49)
+    return fail(FMM_ERR_UNSUPPORTED, "fmm_linear_noalloc: scheme " + std::to_string(scheme) +
+                                         " is not a BF16 linear scheme (7, 48 or 49)");
   fmm_dims d;
   if (int rc = dims_for(scheme, M, K, N, &d)) return rc;
   if (A == nullptr || W == nullptr || C == nullptr)

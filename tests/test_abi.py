@@ -61,6 +61,13 @@ def test_host_side_errors_need_no_gpu():
     fake = ctypes.c_void_p(0x1000)
     rc = lib.fmm_linear_noalloc(7, fake, fake, None, fake, 8192, 8192, 8192, None)
     assert rc == _native.FMM_ERR_TOO_LARGE
+    # rank 343 has no BF16 form: refused up front, naming the entry point
+    rc = lib.fmm_linear_noalloc(343, fake, fake, None, fake, 64, 64, 64, None)
+    assert rc == _native.FMM_ERR_UNSUPPORTED
+    assert "fmm_linear_noalloc" in _native.last_error()
+    # 32 MiB + 256 B of planes (rank 7, 166 x 2704 x 3184): refused before any launch
+    rc = lib.fmm_linear_noalloc(7, fake, fake, None, fake, 166, 2704, 3184, None)
+    assert rc == _native.FMM_ERR_TOO_LARGE
     with pytest.raises(ValueError, match="unknown scheme"):
         _native.check(lib.fmm_plan_dims(3, 4, 4, 4, ctypes.byref(dims)), "fmm_plan_dims")
 

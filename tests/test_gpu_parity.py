@@ -191,11 +191,15 @@ def test_linear_matches_oracle(name, shape):
     assert oracle.relative_l2(got, ref) < 5e-3
 
 
-@pytest.mark.parametrize("name,limit", [("rank7", 1.2), ("rank48", 1.2), ("rank49", 2.0)])
+@pytest.mark.parametrize("name,limit", [("rank7", 1.2), ("rank48", 1.2),
+                                        pytest.param("rank49", 2.0, id="rank49-declared-gate-failure")])
 def test_error_gate_against_fp64(name, limit):
-    """Config-1 distributions (A~N(0,1), W~N(0,0.02)); rank 49 is reported
-    with its known ~1.7x ratio and bounded at 2x (the 1.2x gate is arithmetically
-    out of reach for it with FP16 leaves)."""
+    """Config-1 distributions (A~N(0,1), W~N(0,0.02)).  Rank 7 and rank 48
+    pass the 1.2x gate.  Rank 49 with FP16 leaves is a declared gate failure
+    (~1.7x native BF16: its two-level transforms round larger sums to FP16);
+    the benchmark configuration that names it runs rank 48 instead, and the
+    bound of 2x here only catches regressions.  The full-size gate per
+    configuration is ``test_gpu_error_gate.py``."""
     M, K, N = 512, 1024, 1024
     A, W, _ = make_linear_inputs(M, K, N, seed=0)
     exact = f32(A).astype(np.float64) @ f32(W).astype(np.float64).T
