@@ -1,52 +1,72 @@
-"""Inductor ``external_matmul`` callable (reference ``external_mm.py:1-48``).
+"""Inductor ``external_matmul`` callable (the reference's
+``src/rdna3_fastmm/external_mm.py``).
 
-``rdna3_rank49_dynamic_v1_out(left, right, *, out)`` is offered to Inductor's
-GEMM autotuner.  It runs ``Rank49Plan.run`` only for FP16 ``left @ right``
-shapes in ``Rank49Plan.dynamic_shapes`` (the plain-mm API's measured table)
-and when the workspace fits in free memory; every other call is
-``torch.mm(left, right, out=out)``, exactly as in the reference.  No plain-mm
-shape beats cuBLAS on B200, so that table is empty and the callable is the
-library product for every shape.
+Inductor's GEMM autotuner may call ``rdna3_rank49_dynamic_v1_out(left, right,
+*, out)`` for any ``mm`` it lowers.  The callable asks the rank-49 plan
+itself whether it takes the call, instead of restating the plan's rules:
+
+1. the plan's gate (``Rank49Plan.is_recommended``: FP16 operands and FP16
+   leaves, a shape in the plan's measured ``dynamic_shapes`` table, the
+   tested runtime) decides whether the shape goes to the B200 kernels at all;
+2. constructing the plan and ``plan.run`` validate device, dtype, layout,
+   autograd and storage overlap, raising ``ValueError`` before any launch;
+3. ``allocate_workspace`` raises ``MemoryError`` when the planes do not fit
+   in free device memory.
+
+Whatever the plan refuses (and every call with autograd recording) becomes
+``torch.mm(left, right, out=out)``.  No plain-mm shape beats cuBLAS on B200,
+so the measured table is empty and every call is the library product.
 """
 
 from __future__ import annotations
 
 import torch
 
-from .runtime import Rank49Plan, is_tested_runtime
+from .runtime import Rank49Plan
+
+__all__ = ["is_rank49_dynamic_eligible", "rdna3_rank49_dynamic_v1_out"]
+
+
+def _plan_for(left: torch.Tensor, right: torch.Tensor) -> Rank49Plan | None:
+    """A rank-49 plan for ``left @ right`` when the plan's gate admits it."""
+    if torch.is_grad_enabled() or left.dim() != 2 or right.dim() != 2:
+        return None
+    shape = (left.shape[0], left.shape[1], right.shape[1])
+    if shape not in Rank49Plan.dynamic_shapes:  # cheap first: no plan for unmeasured shapes
+        return None
+    try:
+        plan = Rank49Plan(*shape, left.device, left.dtype)
+    except ValueError:  # not a CUDA device, or a precision pair the plan lacks
+        return None
+    return plan if plan.is_recommended() else None
+
+
+def _validated(plan: Rank49Plan, left: torch.Tensor, right: torch.Tensor, out: torch.Tensor) -> bool:
+    try:
+        plan._validate_left(left)
+        plan._validate_right(right)
+        plan._output(out)
+        plan._validate_output_storage(out, left, right)
+    except ValueError:
+        return False
+    return True
 
 
 def is_rank49_dynamic_eligible(left: torch.Tensor, right: torch.Tensor, out: torch.Tensor) -> bool:
-    if torch.is_grad_enabled():
-        return False
-    if left.ndim != 2 or right.ndim != 2 or out.ndim != 2:
-        return False
-    rows, inner = left.shape
-    right_inner, columns = right.shape
-    if inner != right_inner or tuple(out.shape) != (rows, columns):
-        return False
-    if (rows, inner, columns) not in getattr(Rank49Plan, "dynamic_shapes", frozenset()):
-        return False
-    if left.dtype != torch.float16 or right.dtype != left.dtype or out.dtype != left.dtype:
-        return False
-    if left.device != right.device or out.device != left.device:
-        return False
-    if not (left.is_contiguous() and right.is_contiguous() and out.is_contiguous()):
-        return False
-    if left.requires_grad or right.requires_grad or out.requires_grad:
-        return False
-    return left.device.type == "cuda" and is_tested_runtime(left.device)
+    """Whether ``rdna3_rank49_dynamic_v1_out`` runs the B200 plan for these
+    tensors (memory permitting)."""
+    plan = _plan_for(left, right)
+    return plan is not None and _validated(plan, left, right, out)
 
 
 def rdna3_rank49_dynamic_v1_out(left: torch.Tensor, right: torch.Tensor, *, out: torch.Tensor) -> None:
-    if not is_rank49_dynamic_eligible(left, right, out):
-        torch.mm(left, right, out=out)
-        return
-    rows, inner = left.shape
-    columns = right.shape[1]
-    plan = Rank49Plan(rows, inner, columns, left.device, left.dtype)
-    free_bytes, _ = torch.cuda.mem_get_info(left.device)
-    if plan.workspace_bytes > free_bytes:
-        torch.mm(left, right, out=out)
-        return
-    plan.run(left, right, plan.allocate_workspace(max_free_memory_fraction=1.0), out)
+    plan = _plan_for(left, right)
+    if plan is not None and _validated(plan, left, right, out):
+        try:
+            workspace = plan.allocate_workspace(max_free_memory_fraction=1.0)
+        except MemoryError:
+            workspace = None
+        if workspace is not None:
+            plan.run(left, right, workspace, out)
+            return
+    torch.mm(left, right, out=out)

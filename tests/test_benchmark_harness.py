@@ -271,3 +271,31 @@ def test_model_shape_corpus_matches_reference_case_ids():
     case = corpus.case("ideogram4-local-8214-mlp-up")
     command = benchmark_command(case, _config(), Path("results/case.json"))
     assert command[command.index("--shape") + 1] == "8214,4608,12288" and "--no-bias" in command
+
+
+def test_runner_keeps_going_after_a_failed_case(tmp_path: Path, monkeypatch):
+    """Every selected case runs; the run record names each outcome and the
+    exit status reports the failure."""
+    import sys as _sys
+
+    from benchmarks import run_corpus
+
+    def fake_command(case, config, output_path):
+        code = 3 if case.id == "square-8192" else 0
+        return [_sys.executable, "-c", f"import sys; sys.exit({code})"]
+
+    monkeypatch.setattr(run_corpus, "benchmark_command", fake_command)
+    status = run_corpus.main(["--case", "square-8192", "--case", "dit-4096-mlp-up",
+                              "--output-directory", str(tmp_path), "--algorithm", "rank7"])
+    assert status == 1
+    record = json.loads((tmp_path / "run-rank7.json").read_text())
+    outcomes = {c["case"]: (c["status"], c["returncode"]) for c in record["cases"]}
+    assert outcomes == {"square-8192": ("failed", 3), "dit-4096-mlp-up": ("ok", 0)}
+    assert record["cases"][1]["output"].endswith("dit-4096-mlp-up-rank7.json")
+
+
+def test_runner_lists_every_invalid_setting_at_once(capsys):
+    with pytest.raises(SystemExit):
+        parse_arguments(["--case", "a", "--output-directory", "out", "--warmups", "0", "--rounds", "2"])
+    err = capsys.readouterr().err
+    assert "--warmups" in err and "--rounds" in err

@@ -82,3 +82,18 @@ def test_default_mode_resolves_to_default_options(monkeypatch):
     assert captured["options"] == {}
     inductor.compile_backend(gm, [torch.randn(4)], mode="reduce-overhead")
     assert captured["options"] == {"triton.cudagraphs": True}
+
+
+def test_external_mm_admitted_shape_on_cpu_falls_back(monkeypatch):
+    """A shape in the plan's table still goes to torch.mm when the plan itself
+    refuses the tensors (here: a CPU device)."""
+    from rdna3_fastmm.runtime import Rank49Plan
+
+    monkeypatch.setattr(Rank49Plan, "dynamic_shapes", frozenset({(8, 6, 5)}))
+    left = torch.randn(8, 6, dtype=torch.float16)
+    right = torch.randn(6, 5, dtype=torch.float16)
+    out = torch.empty(8, 5, dtype=torch.float16)
+    with torch.no_grad():
+        assert not external_mm.is_rank49_dynamic_eligible(left, right, out)
+        external_mm.rdna3_rank49_dynamic_v1_out(left, right, out=out)
+    torch.testing.assert_close(out, torch.mm(left, right))
