@@ -11,7 +11,8 @@
  *   - all pointers are caller-owned device pointers; nothing is allocated,
  *     freed, retained or synchronised (work is queued on `stream`);
  *   - BF16 tensors are row-major with the given leading dimension in
- *     elements; FP16 planes are stacked [rank][rows][pitch] with
+ *     elements; planes (FP16, or BF16 with FMM_DTYPE_BF16_BF16) are stacked
+ *     [rank][rows][pitch] with
  *     pitch = round_up(cols, 8) elements (fmm_plan_dims), which keeps every
  *     row 16-byte aligned for TMA; plane buffers must be 16-byte aligned;
  *   - the return value is FMM_OK or an FMM_ERR_* code; fmm_last_error_string
@@ -54,9 +55,19 @@ typedef struct CUstream_st* fmm_stream_t; /* == cudaStream_t */
 /* bits of the device status word */
 #define FMM_STATUS_TIMEOUT 1u
 
-/* element types of A, weight/B, bias and C (the planes are always FP16) */
+/* precision of a call (the `dtype` argument): the element type of A,
+ * weight/B, bias and C, and of the L, Rt and P planes.
+ *   FMM_DTYPE_BF16       BF16 operands and output, FP16 planes
+ *                        (the reference's (bfloat16, float16) precision pair)
+ *   FMM_DTYPE_F16        FP16 operands, output and planes
+ *                        (the reference's (float16, float16) pair)
+ *   FMM_DTYPE_BF16_BF16  BF16 operands, output and planes -- rank 49 only,
+ *                        the reference's (bfloat16, bfloat16) pair of
+ *                        Rank49Plan (src/rdna3_fastmm/runtime.py:852-858);
+ *                        FMM_ERR_UNSUPPORTED for the other schemes */
 #define FMM_DTYPE_BF16 0
 #define FMM_DTYPE_F16 1
+#define FMM_DTYPE_BF16_BF16 2
 
 /* fmm_linear flags */
 #define FMM_LINEAR_PREPACKED 1u /* `Rt` already holds the packed right planes; W is ignored */
@@ -83,13 +94,14 @@ const char* fmm_last_error_string(void);
  * Replaces MatrixShape.from_dimensions (src/rdna3_fastmm/runtime.py:56-89). */
 int fmm_plan_dims(int scheme, int64_t M, int64_t K, int64_t N, fmm_dims* out);
 
-/* A[M,K] (BF16 or FP16 per dtype, lda) -> L[R][bm][ldk] (FP16).
+/* A[M,K] (BF16 or FP16 per dtype, lda) -> L[R][bm][ldk] (FP16, or BF16 for
+ * FMM_DTYPE_BF16_BF16).
  * Replaces left_transform_kernel (src/rdna3_fastmm/runtime.py:597-615;
  * src/rdna3_fastmm/generated/rank7_2x2x2.py:9-62 and the rank-48/49 twins). */
 int fmm_transform_a(int scheme, int dtype, const void* A, int64_t M, int64_t K, int64_t lda,
                     void* L, fmm_stream_t stream);
 
-/* weight[N,K] (dtype, ldw) -> Rt[R][bn][ldk] (FP16), the transform of
+/* weight[N,K] (dtype, ldw) -> Rt[R][bn][ldk] (planes per dtype), the transform of
  * B = weight^T stored K-major.  Used per call (dynamic) and once (prepack).
  * Replaces right_transform_weight_kernel (src/rdna3_fastmm/runtime.py:637-655;
  * src/rdna3_fastmm/generated/rank7_2x2x2.py:121-204 and twins). */
@@ -106,7 +118,7 @@ int fmm_transform_w(int scheme, int dtype, const void* W, int64_t N, int64_t K, 
 int fmm_transform_aw(int scheme, int dtype, const void* A, int64_t M, int64_t K, int64_t lda,
                      void* L, const void* W, int64_t N, int64_t ldw, void* Rt, fmm_stream_t stream);
 
-/* Contiguous right matrix B[K,N] (dtype, ldb) -> Rt[R][bn][ldk] (FP16), the
+/* Contiguous right matrix B[K,N] (dtype, ldb) -> Rt[R][bn][ldk] (planes per dtype), the
  * same planes as fmm_transform_w of weight = B^T (transposed on chip).  The
  * plain-mm API, per call and for pack_right.
  * Replaces right_transform_kernel (src/rdna3_fastmm/runtime.py:617-635;
@@ -120,7 +132,16 @@ int fmm_transform_b(int scheme, int dtype, const void* B, int64_t K, int64_t N, 
 int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
                   void* P, fmm_stream_t stream);
 
-/* P[R][bm][ldp] (FP16) -> C[M,N] (dtype, ldc) with optional bias[N] (dtype,
+/* fmm_leaf_gemm with BF16 planes: BF16 L and Rt, FP32 accumulation in tensor
+ * memory, BF16 products (round to nearest even) -- the leaf products of the
+ * FMM_DTYPE_BF16_BF16 precision.
+ * Replaces torch.bmm(L, Rw, out=P) on BF16 planes, which the reference runs
+ * for Rank49Plan's (bfloat16, bfloat16) pair (src/rdna3_fastmm/runtime.py:728-732,
+ * 852-858). */
+int fmm_leaf_gemm_bf16(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
+                       void* P, fmm_stream_t stream);
+
+/* P[R][bm][ldp] (planes per dtype) -> C[M,N] (dtype, ldc) with optional bias[N] (dtype,
  * may be NULL): FP32 recombination, bias added last, round to nearest even.
  * Replaces output_transform_kernel / output_transform_bias_kernel
  * (src/rdna3_fastmm/runtime.py:657-698). */

@@ -23,6 +23,12 @@ It restates, in numpy, the algorithm of chelokot/rdna3-fastmm for one
    FP16 square rank-343 scheme, a +-1 coefficient sum with an FP16 store
    (``generated/rank343_8x8x8.py`` ``output_transform_mfma_kernel``).
 
+Planes are FP16 by default.  ``planes="bf16"`` gives the reference's
+``(bfloat16, bfloat16)`` precision pair of ``Rank49Plan``
+(``src/rdna3_fastmm/runtime.py:852-858``): the same FP32 arithmetic, with
+every plane and product rounded to BF16 (nearest even) instead; BF16 planes
+are returned as float32 arrays holding BF16 values.
+
 Every gate and output is evaluated with the association written in the
 certificate (left to right over signed terms for reduced circuits, the parsed
 expression tree for SLP lines), which is the order the reference kernels use,
@@ -174,28 +180,39 @@ def _blocks(src: np.ndarray, s: int, bh: int, bw: int) -> list[np.ndarray]:
     return [padded[i * bh:(i + 1) * bh, j * bw:(j + 1) * bw] for i in range(s) for j in range(s)]
 
 
-def left_transform(name: str, A: np.ndarray) -> np.ndarray:
-    """A [M, K] (bf16 values as float32) -> L [R, bm, bk] float16."""
+def round_plane(x: np.ndarray, planes: str = "fp16") -> np.ndarray:
+    """FP32 plane values rounded to the plane format (nearest even): float16,
+    or float32 holding BF16 values for ``planes="bf16"``."""
+    if planes == "fp16":
+        return np.asarray(x, dtype=np.float32).astype(np.float16)
+    if planes == "bf16":
+        return bf16_round(np.asarray(x, dtype=np.float32))
+    raise ValueError(f"unknown plane format {planes!r}")
+
+
+def left_transform(name: str, A: np.ndarray, planes: str = "fp16") -> np.ndarray:
+    """A [M, K] (bf16 values as float32) -> L [R, bm, bk] planes."""
     s, rank, left, _, _ = scheme_circuits(name)
     M, K = A.shape
     bm, bk = -(-M // s), -(-K // s)
     outs = left.evaluate(_blocks(A.astype(np.float32), s, bm, bk))
-    return np.stack([o.astype(np.float16) for o in outs])
+    return np.stack([round_plane(o, planes) for o in outs])
 
 
-def weight_transform(name: str, W: np.ndarray) -> np.ndarray:
-    """weight [N, K] -> R [R, bk, bn] float16 (transform of B = weight^T)."""
+def weight_transform(name: str, W: np.ndarray, planes: str = "fp16") -> np.ndarray:
+    """weight [N, K] -> R [R, bk, bn] planes (transform of B = weight^T)."""
     s, rank, _, right, _ = scheme_circuits(name)
     B = np.ascontiguousarray(W.astype(np.float32).T)
     K, N = B.shape
     bk, bn = -(-K // s), -(-N // s)
     outs = right.evaluate(_blocks(B, s, bk, bn))
-    return np.stack([o.astype(np.float16) for o in outs])
+    return np.stack([round_plane(o, planes) for o in outs])
 
 
-def leaf_products(L: np.ndarray, R: np.ndarray) -> np.ndarray:
-    """FP16 planes -> FP16 products, accumulated in float64 then rounded."""
-    return np.matmul(L.astype(np.float64), R.astype(np.float64)).astype(np.float16)
+def leaf_products(L: np.ndarray, R: np.ndarray, planes: str = "fp16") -> np.ndarray:
+    """Planes -> products in the plane format, accumulated in float64 then
+    rounded (through float32 for BF16)."""
+    return round_plane(np.matmul(L.astype(np.float64), R.astype(np.float64)), planes)
 
 
 @lru_cache(maxsize=None)
@@ -223,7 +240,8 @@ def _coefficient_sum(name: str, P: np.ndarray) -> list[np.ndarray]:
 
 def output_transform(name: str, P: np.ndarray, M: int, N: int,
                      bias: np.ndarray | None = None, out_dtype: str = "bf16") -> np.ndarray:
-    """P [R, bm, bn] float16 -> C [M, N] as float32 holding bf16 values
+    """P [R, bm, bn] (float16, or float32 holding BF16 products) -> C [M, N]
+    as float32 holding bf16 values
     (``out_dtype="fp16"``: FP16 values, the reference's FP16-plan output)."""
     s, rank, _, _, output = scheme_circuits(name)
     bm, bn = P.shape[1], P.shape[2]
@@ -245,11 +263,11 @@ def output_transform(name: str, P: np.ndarray, M: int, N: int,
 
 
 def linear(name: str, A: np.ndarray, W: np.ndarray, bias: np.ndarray | None = None,
-           products=leaf_products) -> np.ndarray:
+           products=leaf_products, planes: str = "fp16") -> np.ndarray:
     """Whole path: ``F.linear(A, W, bias)`` as the reduced-rank algorithm."""
-    L = left_transform(name, A)
-    R = weight_transform(name, W)
-    P = products(L, R)
+    L = left_transform(name, A, planes)
+    R = weight_transform(name, W, planes)
+    P = products(L, R) if planes == "fp16" else products(L, R, planes)
     return output_transform(name, P, A.shape[0], W.shape[0], bias)
 
 

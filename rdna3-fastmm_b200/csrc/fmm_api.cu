@@ -213,7 +213,7 @@ TransformArgs transform_args(const void* src, int64_t rows, int64_t cols, int64_
   a.rows = rows;
   a.cols = cols;
   a.ld = ld;
-  a.dst = static_cast<__half*>(dst);
+  a.dst = static_cast<uint16_t*>(dst);
   a.brows = brows;
   a.bcols = bcols;
   a.ldd = ldd;
@@ -221,16 +221,26 @@ TransformArgs transform_args(const void* src, int64_t rows, int64_t cols, int64_
   return a;
 }
 
-template <int SCHEME, bool kWeight, bool kHalf>
+// Precision of one launch (the dtype argument of the C ABI): operand and
+// output elements FP16 or BF16, plane elements BF16 only for
+// FMM_DTYPE_BF16_BF16 (FP16 otherwise).
+template <int PREC>
+struct Precision {
+  static constexpr bool kHalf = PREC == FMM_DTYPE_F16;
+  static constexpr bool kBfPlanes = PREC == FMM_DTYPE_BF16_BF16;
+};
+
+template <int SCHEME, bool kWeight, int PREC>
 int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t ld, void* dst,
                            int64_t brows, int64_t bcols, int64_t ldd, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
+  constexpr bool kHalf = Precision<PREC>::kHalf, kBf = Precision<PREC>::kBfPlanes;
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
   const TransformArgs a = transform_args<SCHEME>(src, rows, cols, ld, dst, brows, bcols, ldd);
   const int64_t items = brows * (ldd / T::VEC);
   using Prog = typename std::conditional<kWeight, typename T::Right, typename T::Left>::type;
-  block_transform_kernel<Prog, T::S, T::VEC, kWeight, T::kInThreads, T::kInBlocks, kHalf>
+  block_transform_kernel<Prog, T::S, T::VEC, kWeight, T::kInThreads, T::kInBlocks, kHalf, kBf>
       <<<streaming_grid(info, items, T::kInThreads, T::kInGrid), T::kInThreads, 0, stream>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, kWeight ? "weight transform launch" : "left transform launch");
@@ -239,10 +249,11 @@ int launch_input_transform(const void* src, int64_t rows, int64_t cols, int64_t 
 
 // Left and weight transform of a dynamic linear in one launch; each gets a
 // share of the CTAs proportional to its vectors (at least one).
-template <int SCHEME, bool kHalf>
+template <int SCHEME, int PREC>
 int launch_paired_transform(const void* A, int64_t M, int64_t K, int64_t lda, void* L, const void* W,
                             int64_t N, int64_t ldw, void* Rt, const fmm_dims& d, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
+  constexpr bool kHalf = Precision<PREC>::kHalf, kBf = Precision<PREC>::kBfPlanes;
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
   const TransformArgs left = transform_args<SCHEME>(A, M, K, lda, L, d.bm, d.bk, d.ldk);
@@ -255,7 +266,7 @@ int launch_paired_transform(const void* A, int64_t M, int64_t K, int64_t lda, vo
   if (left_blocks < 1) left_blocks = 1;
   if (left_blocks > total - 1) left_blocks = total - 1;
   paired_transform_kernel<typename T::Left, typename T::Right, T::S, T::VEC, T::kInThreads,
-                          T::kInBlocks, kHalf>
+                          T::kInBlocks, kHalf, kBf>
       <<<total, T::kInThreads, 0, stream>>>(left, weight, static_cast<uint32_t>(left_blocks));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "paired transform launch");
@@ -266,7 +277,7 @@ template <class Coefs, bool kHalf>
 int launch_reconstruct_tc(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                           void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream);
 
-template <int SCHEME, bool kHalf>
+template <int SCHEME, int PREC>
 int launch_reconstruct_staged(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                               void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream);
 
@@ -277,10 +288,11 @@ bool staged_reconstruct_enabled() {
   return v == nullptr || std::string(v) != "register";
 }
 
-template <int SCHEME, bool kHalf>
+template <int SCHEME, int PREC>
 int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                        void* C, int64_t ldc, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
+  constexpr bool kHalf = Precision<PREC>::kHalf, kBf = Precision<PREC>::kBfPlanes;
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
   if constexpr (T::kTensorCoreOutput) {
@@ -288,16 +300,16 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
   } else {
     if constexpr (T::kOutStages > 0) {
       if (staged_reconstruct_enabled() && aligned(P, 16) && d.ldp % 8 == 0)
-        return launch_reconstruct_staged<SCHEME, kHalf>(P, d, M, N, bias, C, ldc, info, stream);
+        return launch_reconstruct_staged<SCHEME, PREC>(P, d, M, N, bias, C, ldc, info, stream);
     }
     constexpr int V = T::kOutVec;
     const bool vec = (d.bn % V == 0) && (ldc % V == 0) && aligned(C, 2 * V);
     const bool vec_bias = (d.bn % V == 0) && bias != nullptr && aligned(bias, 2 * V);
     const int64_t items = d.bm * ceil_div(d.bn, V);
     const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
-    reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
+    reconstruct_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf, kBf>
         <<<grid, T::kOutThreads, 0, stream>>>(
-            static_cast<const __half*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
+            static_cast<const uint16_t*>(P), d.bm, d.bn, d.ldp, static_cast<const uint16_t*>(bias),
             static_cast<uint16_t*>(C), M, N, ldc, (vec ? 1 : 0) | (vec_bias ? 2 : 0));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "reconstruct launch");
@@ -305,11 +317,12 @@ int launch_reconstruct(const void* P, const fmm_dims& d, int64_t M, int64_t N, c
   }
 }
 
-template <int SCHEME, bool kHalf>
+template <int SCHEME, int PREC>
 int launch_reconstruct_gather(const void* P, const fmm_dims& d, int64_t M, int64_t N,
                               const void* bias, const GatherDests& dests, int64_t ldc,
                               cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
+  constexpr bool kHalf = Precision<PREC>::kHalf, kBf = Precision<PREC>::kBfPlanes;
   if constexpr (T::kTensorCoreOutput) {
     return fail(FMM_ERR_UNSUPPORTED, "the gathering reconstruct covers the circuit schemes (7, 48, 49)");
   } else {
@@ -321,8 +334,8 @@ int launch_reconstruct_gather(const void* P, const fmm_dims& d, int64_t M, int64
     const bool vec_bias = (d.bn % V == 0) && bias != nullptr && aligned(bias, 2 * V);
     const int64_t items = d.bm * ceil_div(d.bn, V);
     const int grid = streaming_grid(info, items, T::kOutThreads, T::kOutGrid);
-    reconstruct_gather_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf>
-        <<<grid, T::kOutThreads, 0, stream>>>(static_cast<const __half*>(P), d.bm, d.bn, d.ldp,
+    reconstruct_gather_kernel<typename T::Output, T::S, V, T::kOutThreads, T::kOutBlocks, kHalf, kBf>
+        <<<grid, T::kOutThreads, 0, stream>>>(static_cast<const uint16_t*>(P), d.bm, d.bn, d.ldp,
                                               static_cast<const uint16_t*>(bias), dests, M, N, ldc,
                                               (vec ? 1 : 0) | (vec_bias ? 2 : 0));
     cudaError_t e = cudaGetLastError();
@@ -334,14 +347,15 @@ int launch_reconstruct_gather(const void* P, const fmm_dims& d, int64_t M, int64
 template <class Kernel>
 int ensure_smem_attribute(bool& done, Kernel kernel, size_t bytes);
 
-template <int SCHEME, bool kHalf>
+template <int SCHEME, int PREC>
 int launch_right_kn(const void* B, int64_t K, int64_t N, int64_t ldb, void* dst, const fmm_dims& d,
                     cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
+  constexpr bool kHalf = Precision<PREC>::kHalf, kBf = Precision<PREC>::kBfPlanes;
   constexpr int TK = T::kKnTK, TN = T::kKnTN;
   using Tile = KnTile<T::S, TK, TN>;
   auto kernel = right_transform_kn_kernel<typename T::Right, T::S, kHalf, TK, TN, T::kKnVec, T::kKnThreads,
-                                           T::kKnBlocks>;
+                                           T::kKnBlocks, kBf>;
   static bool configured[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -352,66 +366,74 @@ int launch_right_kn(const void* B, int64_t K, int64_t N, int64_t ldb, void* dst,
   const dim3 grid(static_cast<unsigned>(ceil_div(d.ldk, TK)), static_cast<unsigned>(ceil_div(d.bn, TN)));
   const bool vec = (ldb % 8 == 0) && (d.bn % 8 == 0) && aligned(B, 16);
   kernel<<<grid, T::kKnThreads, Tile::kBytes, stream>>>(static_cast<const uint16_t*>(B), K, N, ldb,
-                                                        static_cast<__half*>(dst), d.bk, d.bn, d.ldk,
+                                                        static_cast<uint16_t*>(dst), d.bk, d.bn, d.ldk,
                                                         vec ? 1 : 0);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "right transform (K x N) launch");
   return FMM_OK;
 }
 
-// Runtime (scheme, dtype) -> template instance.
-template <template <int, bool> class F, class... Args>
+// Runtime (scheme, dtype) -> template instance.  BF16 planes exist for rank 49
+// only, the one scheme whose reference plan offers them (Rank49Plan's
+// (bfloat16, bfloat16) precision pair).
+template <template <int, int> class F, class... Args>
 int dispatch(int scheme, int dtype, Args... args) {
   const bool half = dtype == FMM_DTYPE_F16;
+  if (dtype == FMM_DTYPE_BF16_BF16 && scheme != FMM_SCHEME_RANK49)
+    return fail(FMM_ERR_UNSUPPORTED, "BF16 planes (FMM_DTYPE_BF16_BF16) are offered for rank 49 only");
   switch (scheme) {
     case FMM_SCHEME_RANK7:
-      return half ? F<FMM_SCHEME_RANK7, true>::run(args...) : F<FMM_SCHEME_RANK7, false>::run(args...);
+      return half ? F<FMM_SCHEME_RANK7, FMM_DTYPE_F16>::run(args...)
+                  : F<FMM_SCHEME_RANK7, FMM_DTYPE_BF16>::run(args...);
     case FMM_SCHEME_RANK48:
-      return half ? F<FMM_SCHEME_RANK48, true>::run(args...) : F<FMM_SCHEME_RANK48, false>::run(args...);
+      return half ? F<FMM_SCHEME_RANK48, FMM_DTYPE_F16>::run(args...)
+                  : F<FMM_SCHEME_RANK48, FMM_DTYPE_BF16>::run(args...);
     case FMM_SCHEME_RANK343:
       // FP16 inputs and output only, as the reference plan (precision_pairs)
       if (!half) return fail(FMM_ERR_UNSUPPORTED, "rank 343 takes FP16 operands only");
-      return F<FMM_SCHEME_RANK343, true>::run(args...);
+      return F<FMM_SCHEME_RANK343, FMM_DTYPE_F16>::run(args...);
     default:
-      return half ? F<FMM_SCHEME_RANK49, true>::run(args...) : F<FMM_SCHEME_RANK49, false>::run(args...);
+      if (dtype == FMM_DTYPE_BF16_BF16) return F<FMM_SCHEME_RANK49, FMM_DTYPE_BF16_BF16>::run(args...);
+      return half ? F<FMM_SCHEME_RANK49, FMM_DTYPE_F16>::run(args...)
+                  : F<FMM_SCHEME_RANK49, FMM_DTYPE_BF16>::run(args...);
   }
 }
-template <int SC, bool H>
+template <int SC, int H>
 struct LeftOp {
   static int run(const void* A, int64_t M, int64_t K, int64_t lda, void* L, const fmm_dims* d,
                  cudaStream_t s) {
     return launch_input_transform<SC, false, H>(A, M, K, lda, L, d->bm, d->bk, d->ldk, s);
   }
 };
-template <int SC, bool H>
+template <int SC, int H>
 struct PairedOp {
   static int run(const void* A, int64_t M, int64_t K, int64_t lda, void* L, const void* W, int64_t N,
                  int64_t ldw, void* Rt, const fmm_dims* d, cudaStream_t s) {
     return launch_paired_transform<SC, H>(A, M, K, lda, L, W, N, ldw, Rt, *d, s);
   }
 };
-template <int SC, bool H>
+template <int SC, int H>
 struct WeightOp {
   static int run(const void* W, int64_t N, int64_t K, int64_t ldw, void* Rt, const fmm_dims* d,
                  cudaStream_t s) {
     return launch_input_transform<SC, true, H>(W, N, K, ldw, Rt, d->bn, d->bk, d->ldk, s);
   }
 };
-template <int SC, bool H>
+template <int SC, int H>
 struct RightKnOp {
   static int run(const void* B, int64_t K, int64_t N, int64_t ldb, void* Rt, const fmm_dims* d,
                  cudaStream_t s) {
     return launch_right_kn<SC, H>(B, K, N, ldb, Rt, *d, s);
   }
 };
-template <int SC, bool H>
+template <int SC, int H>
 struct ReconstructGatherOp {
   static int run(const void* P, const fmm_dims* d, int64_t M, int64_t N, const void* bias,
                  const GatherDests* dests, int64_t ldc, cudaStream_t s) {
     return launch_reconstruct_gather<SC, H>(P, *d, M, N, bias, *dests, ldc, s);
   }
 };
-template <int SC, bool H>
+template <int SC, int H>
 struct ReconstructOp {
   static int run(const void* P, const fmm_dims* d, int64_t M, int64_t N, const void* bias, void* C,
                  int64_t ldc, cudaStream_t s) {
@@ -420,8 +442,9 @@ struct ReconstructOp {
 };
 
 int check_dtype(int dtype) {
-  if (dtype != FMM_DTYPE_BF16 && dtype != FMM_DTYPE_F16)
-    return fail(FMM_ERR_UNSUPPORTED, "dtype must be FMM_DTYPE_BF16 or FMM_DTYPE_F16");
+  if (dtype != FMM_DTYPE_BF16 && dtype != FMM_DTYPE_F16 && dtype != FMM_DTYPE_BF16_BF16)
+    return fail(FMM_ERR_UNSUPPORTED,
+                "dtype must be FMM_DTYPE_BF16, FMM_DTYPE_F16 or FMM_DTYPE_BF16_BF16");
   return FMM_OK;
 }
 
@@ -550,9 +573,14 @@ int ensure_smem_attribute(bool& done, Kernel kernel, size_t bytes) {
   return FMM_OK;
 }
 
-template <class Cfg>
+template <class Cfg, bool kBf16>
 int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_t ldk, int sms,
-                bool& configured, cudaStream_t stream) {
+                cudaStream_t stream) {
+  static bool configured[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
   CUtensorMap map_l, map_r, map_r16;
   if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM)) return rc;
   if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, Cfg::kBN / 2)) return rc;
@@ -560,7 +588,8 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   if (int rc = plane_map(&map_r16, Rt, prm.bk, prm.bn, ldk, prm.rank, 16)) return rc;
   {
     std::lock_guard<std::mutex> lock(g_device_mutex);
-    if (int rc = ensure_smem_attribute(configured, leaf_gemm_pair_kernel<Cfg>, Cfg::kSmemBytes)) return rc;
+    if (int rc = ensure_smem_attribute(configured[dev], leaf_gemm_pair_kernel<Cfg, kBf16>, Cfg::kSmemBytes))
+      return rc;
   }
   const int64_t tiles = int64_t(prm.rank) * ceil_div(prm.bm, Cfg::kTileM) * ceil_div(prm.bn, Cfg::kBN);
   const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
@@ -576,7 +605,7 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg>, map_l, map_r, map_r16, prm);
+  e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg, kBf16>, map_l, map_r, map_r16, prm);
   if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM (pair) launch");
   return FMM_OK;
 }
@@ -653,13 +682,14 @@ int launch_reconstruct_tc(const void* P, const fmm_dims& d, int64_t M, int64_t N
 // TMA-staged reconstruct of a circuit scheme: persistent CTAs, one box of
 // 256 positions x R products per tile (unswizzled, so plane r of a tile sits at
 // r * 256 elements in shared memory), two positions a compute thread.
-template <int SCHEME, bool kHalf>
+template <int SCHEME, int PREC>
 int launch_reconstruct_staged(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                               void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream) {
   using T = SchemeTraits<SCHEME>;
   using Prog = typename T::Output;
   using Cfg = StagedReconstructConfig<Prog, T::kOutStages>;
-  auto kernel = reconstruct_staged_kernel<Prog, T::S, T::kOutStages, kHalf, Cfg::kTP, T::kOutStagedBlocks>;
+  auto kernel = reconstruct_staged_kernel<Prog, T::S, T::kOutStages, Precision<PREC>::kHalf, Cfg::kTP,
+                                          T::kOutStagedBlocks, Precision<PREC>::kBfPlanes>;
   static bool configured[kMaxDevices] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -697,6 +727,36 @@ int launch_reconstruct_staged(const void* P, const fmm_dims& d, int64_t M, int64
   return FMM_OK;
 }
 
+// The 1-SM GEMM (small or ragged leaves).
+template <bool kBf16>
+int launch_single(const void* L, const void* Rt, const LeafGemmParams& prm, int64_t ldk, int sms,
+                  cudaStream_t stream) {
+  static bool configured[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
+  CUtensorMap map_l, map_r;
+  if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM)) return rc;
+  if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, GemmCfg::kBN)) return rc;
+  {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (int rc = ensure_smem_attribute(configured[dev], leaf_gemm_kernel<GemmCfg, kBf16>, GemmCfg::kSmemBytes))
+      return rc;
+  }
+  const int64_t tiles = int64_t(prm.rank) * prm.tiles_m * prm.tiles_n;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  leaf_gemm_kernel<GemmCfg, kBf16><<<grid, kGemmThreads, GemmCfg::kSmemBytes, stream>>>(map_l, map_r, prm);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM launch");
+  return FMM_OK;
+}
+
+// FP16 planes (kBf16 = false) or BF16 planes.  The BF16 form carries the
+// 1-SM and the 256 x 256 pair configurations (the ones the cost model picks
+// for every measured shape); a forced narrower pair variant runs as the
+// 256 x 256 pair there.
+template <bool kBf16>
 int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
                      void* P, cudaStream_t stream) {
   if (rank < 1 || bm < 1 || bn < 1 || bk < 1)
@@ -715,40 +775,25 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   prm.tiles_m = static_cast<int32_t>(ceil_div(bm, kGemmBM));
   prm.tiles_n = static_cast<int32_t>(ceil_div(bn, GemmCfg::kBN));
   prm.group_m = 16;
-  prm.P = static_cast<__half*>(P);
+  prm.P = static_cast<uint16_t*>(P);
   prm.timeout_ns = g_timeout_ns;
   if (int64_t(rank) * ceil_div(bm, kGemmBM) * ceil_div(bn, 128) > (int64_t(1) << 30))
     return fail(FMM_ERR_TOO_LARGE, "too many GEMM tiles");
   const int sms = usable_sms(info);
-  const int variant = choose_variant(rank, bm, bn, sms);
+  int variant = choose_variant(rank, bm, bn, sms);
+  if (kBf16 && (variant == kVariantPair192 || variant == kVariantPair128)) variant = kVariantPair256;
   if (variant == kVariantPair256) {
     // deep leaves: 128-deep k-blocks in 3 stages (half the barrier round trips per
     // FLOP) measured 0.3-2.8 % faster from bk = 3072 up and 1-3 % slower below
-    if (bk >= 3072)
-      return launch_pair<PairCfg256K128>(L, Rt, prm, ldk, sms, info->pair256k128_configured, stream);
-    return launch_pair<PairCfg256>(L, Rt, prm, ldk, sms, info->pair256_configured, stream);
+    if (bk >= 3072) return launch_pair<PairCfg256K128, kBf16>(L, Rt, prm, ldk, sms, stream);
+    return launch_pair<PairCfg256, kBf16>(L, Rt, prm, ldk, sms, stream);
   }
-  if (variant == kVariantPair192)
-    return launch_pair<PairCfg192>(L, Rt, prm, ldk, sms, info->pair192_configured, stream);
-  if (variant == kVariantPair128)
-    return launch_pair<PairCfg128>(L, Rt, prm, ldk, sms, info->pair128_configured, stream);
-  if (variant == kVariantPair256K128)
-    return launch_pair<PairCfg256K128>(L, Rt, prm, ldk, sms, info->pair256k128_configured, stream);
-  CUtensorMap map_l, map_r;
-  if (int rc = plane_map(&map_l, L, bk, bm, ldk, rank, kGemmBM)) return rc;
-  if (int rc = plane_map(&map_r, Rt, bk, bn, ldk, rank, GemmCfg::kBN)) return rc;
-  {
-    std::lock_guard<std::mutex> lock(g_device_mutex);
-    if (int rc = ensure_smem_attribute(info->gemm_configured, leaf_gemm_kernel<GemmCfg>,
-                                       GemmCfg::kSmemBytes))
-      return rc;
+  if (variant == kVariantPair256K128) return launch_pair<PairCfg256K128, kBf16>(L, Rt, prm, ldk, sms, stream);
+  if constexpr (!kBf16) {
+    if (variant == kVariantPair192) return launch_pair<PairCfg192, false>(L, Rt, prm, ldk, sms, stream);
+    if (variant == kVariantPair128) return launch_pair<PairCfg128, false>(L, Rt, prm, ldk, sms, stream);
   }
-  const int64_t tiles = int64_t(rank) * prm.tiles_m * prm.tiles_n;
-  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  leaf_gemm_kernel<GemmCfg><<<grid, kGemmThreads, GemmCfg::kSmemBytes, stream>>>(map_l, map_r, prm);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM launch");
-  return FMM_OK;
+  return launch_single<kBf16>(L, Rt, prm, ldk, sms, stream);
 }
 
 // Device address of g_noalloc_scratch on the current device.  In host code the
@@ -851,7 +896,14 @@ int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t b
                   void* P, fmm_stream_t stream) {
   if (L == nullptr || Rt == nullptr || P == nullptr)
     return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
-  return launch_leaf_gemm(rank, L, Rt, bm, bn, bk, P, reinterpret_cast<cudaStream_t>(stream));
+  return launch_leaf_gemm<false>(rank, L, Rt, bm, bn, bk, P, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fmm_leaf_gemm_bf16(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
+                       void* P, fmm_stream_t stream) {
+  if (L == nullptr || Rt == nullptr || P == nullptr)
+    return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  return launch_leaf_gemm<true>(rank, L, Rt, bm, bn, bk, P, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, const void* bias,
@@ -906,7 +958,10 @@ int fmm_linear(int scheme, int dtype, const void* A, const void* W, const void* 
       if (int rc = fmm_transform_b(scheme, dtype, W, K, N, N, Rt, stream)) return rc;
     }
   }
-  if (int rc = fmm_leaf_gemm(static_cast<int>(d.rank), L, Rt, d.bm, d.bn, d.bk, P, stream)) return rc;
+  const int gemm = dtype == FMM_DTYPE_BF16_BF16
+                       ? fmm_leaf_gemm_bf16(static_cast<int>(d.rank), L, Rt, d.bm, d.bn, d.bk, P, stream)
+                       : fmm_leaf_gemm(static_cast<int>(d.rank), L, Rt, d.bm, d.bn, d.bk, P, stream);
+  if (gemm != FMM_OK) return gemm;
   return fmm_reconstruct(scheme, dtype, P, M, N, bias, C, N, stream);
 }
 

@@ -261,6 +261,28 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n) {
   return (1u << 4) | (0u << 7) | (0u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// kind::f16 with BF16 A and B (operand formats, bits 7-9 and 10-12, = 1).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n) {
+  return idesc_f16_f32(m, n) | (1u << 7) | (1u << 10);
+}
+template <bool kBf16>
+__host__ __device__ constexpr uint32_t idesc_kind_f16(uint32_t m, uint32_t n) {
+  return kBf16 ? idesc_bf16_f32(m, n) : idesc_f16_f32(m, n);
+}
+
+// Two FP32 values -> one word of two 16-bit elements (FP16 or BF16), round to
+// nearest even, the first value in the low half.
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2_rn(float lo, float hi) {
+  if constexpr (kBf16) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
 // Same with A MN-major (bit 15: "transpose A"); B stays K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32_a_mn(uint32_t m, uint32_t n) {
   return idesc_f16_f32(m, n) | (1u << 15);

@@ -1,6 +1,8 @@
 // Leaf products of the reduced-rank linear: R independent FP16 GEMMs
 //   P[r][m][n] = sum_k L[r][m][k] * Rt[r][n][k]
-// on the 5th-generation tensor cores (tcgen05) of sm_100a.
+// on the 5th-generation tensor cores (tcgen05) of sm_100a.  With kBf16 the
+// planes and products are BF16 instead (same kind::f16 MMA, BF16 operand
+// formats in the instruction descriptor, BF16 rounding in the epilogue).
 //
 // Structure (one CTA per SM, persistent over the (r, tile_m, tile_n) grid):
 //   warp 0      TMA producer: 3-D tensor maps over the stacked planes, one
@@ -45,7 +47,7 @@ struct LeafGemmParams {
   int32_t rank;
   int32_t tiles_m, tiles_n;
   int32_t group_m;
-  __half* P;
+  uint16_t* P;  // FP16 (or BF16) products
   uint64_t timeout_ns;
 };
 
@@ -76,7 +78,7 @@ __device__ __forceinline__ int tile_n_columns(const LeafGemmParams& p, int tn, i
   return static_cast<int>((rem + granule - 1) / granule * granule);
 }
 
-template <class Cfg>
+template <class Cfg, bool kBf16 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     leaf_gemm_kernel(const __grid_constant__ CUtensorMap tmap_l,
                      const __grid_constant__ CUtensorMap tmap_r, const LeafGemmParams p) {
@@ -183,7 +185,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int r, tm, tn;
         leaf_tile_coords(p, t, r, tm, tn);
         // M = 128, cta_group::1: N a multiple of 16
-        const uint32_t idesc = idesc_f16_f32(kGemmBM, static_cast<uint32_t>(tile_n_columns(p, tn, BN, 16)));
+        const uint32_t idesc =
+            idesc_kind_f16<kBf16>(kGemmBM, static_cast<uint32_t>(tile_n_columns(p, tn, BN, 16)));
         if (!mbar_wait_bounded(tempty_bar + 8 * acc, acc_phase ^ 1u, abort, p.timeout_ns, 2)) {
           ok = false;
           break;
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ready) break;
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tm) * kGemmBM + row_in_tile;
-      __half* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
+      uint16_t* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
       const uint32_t t_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int n_cols = tile_n_columns(p, tn, BN, 16);
@@ -257,11 +260,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int64_t c8 = col + q * 8;
             if (c8 + 8 <= p.ldp) {
               uint4 pk;
-              __half2* h = reinterpret_cast<__half2*>(&pk);
+              uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                h[e] = __floats2half2_rn(__uint_as_float(v[q * 8 + 2 * e]),
-                                         __uint_as_float(v[q * 8 + 2 * e + 1]));
+                w[e] = pack2_rn<kBf16>(__uint_as_float(v[q * 8 + 2 * e]),
+                                       __uint_as_float(v[q * 8 + 2 * e + 1]));
               *reinterpret_cast<uint4*>(prow + c8) = pk;
             }
           }
@@ -331,7 +334,7 @@ struct LeafGemmPairConfig {
   static_assert(BK == 64 || BK == 128, "k-block depth");
 };
 
-template <class Cfg>
+template <class Cfg, bool kBf16 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     leaf_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_l,
                           const __grid_constant__ CUtensorMap tmap_r,
@@ -462,7 +465,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         leaf_tile_coords(q, t, r, tm, tn);
         // M = 256, cta_group::2: N a multiple of 32 (16 columns from each CTA)
         const uint32_t idesc =
-            idesc_f16_f32(Cfg::kTileM, static_cast<uint32_t>(tile_n_columns(q, tn, BN, 32)));
+            idesc_kind_f16<kBf16>(Cfg::kTileM, static_cast<uint32_t>(tile_n_columns(q, tn, BN, 32)));
         if (!mbar_wait_bounded_cluster(tempty_bar + 8 * acc, acc_phase ^ 1u, abort, p.timeout_ns, 12)) {
           ok = false;
           break;
@@ -524,7 +527,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ready) break;
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tm) * Cfg::kTileM + row_in_tile;
-      __half* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
+      uint16_t* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
       const uint32_t t_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int n_cols = tile_n_columns(q, tn, BN, 32);
@@ -540,11 +543,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int64_t c8 = col + g * 8;
             if (c8 + 8 <= p.ldp) {
               uint4 pk;
-              __half2* h = reinterpret_cast<__half2*>(&pk);
+              uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                h[e] = __floats2half2_rn(__uint_as_float(v[g * 8 + 2 * e]),
-                                         __uint_as_float(v[g * 8 + 2 * e + 1]));
+                w[e] = pack2_rn<kBf16>(__uint_as_float(v[g * 8 + 2 * e]),
+                                       __uint_as_float(v[g * 8 + 2 * e + 1]));
               *reinterpret_cast<uint4*>(prow + c8) = pk;
             }
           }

@@ -8,7 +8,9 @@
 // into shared memory per stage, a producer warp keeps STAGES tiles in flight,
 // and TP / 64 compute warps evaluate the same generated circuit on two
 // positions a thread, reading each product from shared memory when the circuit
-// first needs it (under 100 registers, so several CTAs share an SM).  The
+// first needs it (under 100 registers, so several CTAs share an SM).  Product
+// planes are FP16, or BF16 with kBfPlanes (TMA moves them as 2-byte elements
+// either way).  The
 // arithmetic, its order and the rounding are reconstruct_kernel's (the same
 // Prog::run and store_output_vector), so the outputs are bit-identical.
 //
@@ -43,7 +45,8 @@ struct StagedReconstructParams {
   uint64_t timeout_ns;
 };
 
-template <class Prog, int S, int STAGES, bool kHalfOut, int TP = 256, int MIN_BLOCKS = 1>
+template <class Prog, int S, int STAGES, bool kHalfOut, int TP = 256, int MIN_BLOCKS = 1,
+          bool kBfPlanes = false>
 __global__ void __launch_bounds__(StagedReconstructConfig<Prog, STAGES, TP>::kThreads, MIN_BLOCKS)
     reconstruct_staged_kernel(const __grid_constant__ CUtensorMap tmap_p,
                               const StagedReconstructParams p) {
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(StagedReconstructConfig<Prog, STAGES, TP>::kTh
       const uint16_t* tile = tiles + size_t(stage) * Cfg::kR * Cfg::kTP;
       if (j < p.bn) {
         auto in = [&](int r) -> VecF<2> {
-          return unpack_half<2>(*reinterpret_cast<const unsigned*>(tile + r * Cfg::kTP + pos));
+          return unpack_plane<kBfPlanes, 2>(*reinterpret_cast<const unsigned*>(tile + r * Cfg::kTP + pos));
         };
         auto out = [&](int o, const VecF<2>& x) {
           store_output_vector<S, 2, kHalfOut>(o, x, i, j, p.bm, p.bn, p.bias, p.C, p.M, p.N, p.ldc,

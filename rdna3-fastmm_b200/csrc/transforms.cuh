@@ -123,6 +123,24 @@ __device__ __forceinline__ void store_bf16_vec(__nv_bfloat16* p, const VecF<N>& 
   *reinterpret_cast<typename VecIO<N>::BF*>(p) = raw;
 }
 
+// Plane element type: FP16 (kBfPlanes = false) or BF16, round to nearest even.
+template <bool kBfPlanes, int N>
+__device__ __forceinline__ void store_plane_vec(uint16_t* p, const VecF<N>& x) {
+  if constexpr (kBfPlanes) {
+    store_bf16_vec<N>(reinterpret_cast<__nv_bfloat16*>(p), x);
+  } else {
+    store_half_vec<N>(reinterpret_cast<__half*>(p), x);
+  }
+}
+template <bool kBfPlanes, int N>
+__device__ __forceinline__ VecF<N> unpack_plane(const typename VecIO<N>::H& raw) {
+  if constexpr (kBfPlanes) {
+    return unpack_bf16<N>(raw);
+  } else {
+    return unpack_half<N>(raw);
+  }
+}
+
 // Output element (BF16 or FP16), round to nearest even.
 template <bool kHalf>
 __device__ __forceinline__ uint16_t round_out(float x) {
@@ -150,9 +168,9 @@ __device__ __forceinline__ void store_out_vec(uint16_t* p, const VecF<N>& x) {
 }
 
 // ---------------------------------------------------------------------------
-// Input-side transform: src [rows, cols] BF16 (leading dim ld) is cut into
-// S x S zero-padded blocks of [brows, bcols]; Prog combines them into
-// Prog::kOutputs FP16 planes dst[o][brows][ldd].
+// Input-side transform: src [rows, cols] BF16 or FP16 (leading dim ld) is cut
+// into S x S zero-padded blocks of [brows, bcols]; Prog combines them into
+// Prog::kOutputs planes dst[o][brows][ldd], FP16 (or BF16 with kBfPlanes).
 //
 // kWeight = false: activation side, input q is block (q / S, q % S) of A.
 // kWeight = true : weight side; the program's input q is block (q / S, q % S)
@@ -172,19 +190,19 @@ __device__ __forceinline__ void store_out_vec(uint16_t* p, const VecF<N>& x) {
 struct TransformArgs {
   const uint16_t* src;
   int64_t rows, cols, ld;
-  __half* dst;
+  uint16_t* dst;  // FP16 or BF16 plane elements
   int64_t brows, bcols, ldd;
   int vector_loads;
 };
 
 // Body shared by the single and the paired launch: `block` / `blocks` are the
 // CTA index and count this transform owns.
-template <class Prog, int S, int VEC, bool kWeight, bool kHalfIn>
+template <class Prog, int S, int VEC, bool kWeight, bool kHalfIn, bool kBfPlanes>
 __device__ __forceinline__ void block_transform_body(const TransformArgs& a, uint32_t block,
                                                      uint32_t blocks) {
   using Raw = typename VecIO<VEC>::BF;
   const uint16_t* __restrict__ src = a.src;
-  __half* __restrict__ dst = a.dst;
+  uint16_t* __restrict__ dst = a.dst;
   const int64_t rows = a.rows, cols = a.cols, ld = a.ld;
   const int64_t brows = a.brows, bcols = a.bcols, ldd = a.ldd;
   const int vector_loads = a.vector_loads;
@@ -224,16 +242,16 @@ __device__ __forceinline__ void block_transform_body(const TransformArgs& a, uin
     }
     auto in = [&](int q) -> VecF<VEC> { return unpack_in<kHalfIn, VEC>(raw[q]); };
     auto out = [&](int o, const VecF<VEC>& x) {
-      store_half_vec<VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
+      store_plane_vec<kBfPlanes, VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
     };
     Prog::template run<VecF<VEC>>(in, out);
   }
 }
 
 template <class Prog, int S, int VEC, bool kWeight, int THREADS = 256, int MIN_BLOCKS = 1,
-          bool kHalfIn = false>
+          bool kHalfIn = false, bool kBfPlanes = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(const TransformArgs a) {
-  block_transform_body<Prog, S, VEC, kWeight, kHalfIn>(a, blockIdx.x, gridDim.x);
+  block_transform_body<Prog, S, VEC, kWeight, kHalfIn, kBfPlanes>(a, blockIdx.x, gridDim.x);
 }
 
 // The activation-side and the weight-side transform of one dynamic linear in
@@ -241,14 +259,15 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) block_transform_kernel(co
 // weight transform.  Both stream HBM; sharing a launch lets the small left
 // transform's ramp and tail overlap the weight transform instead of
 // serialising with it.
-template <class Left, class Right, int S, int VEC, int THREADS, int MIN_BLOCKS, bool kHalfIn>
+template <class Left, class Right, int S, int VEC, int THREADS, int MIN_BLOCKS, bool kHalfIn,
+          bool kBfPlanes = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) paired_transform_kernel(
     const TransformArgs left, const TransformArgs weight, uint32_t left_blocks) {
   if (blockIdx.x < left_blocks) {
-    block_transform_body<Left, S, VEC, false, kHalfIn>(left, blockIdx.x, left_blocks);
+    block_transform_body<Left, S, VEC, false, kHalfIn, kBfPlanes>(left, blockIdx.x, left_blocks);
   } else {
-    block_transform_body<Right, S, VEC, true, kHalfIn>(weight, blockIdx.x - left_blocks,
-                                                       gridDim.x - left_blocks);
+    block_transform_body<Right, S, VEC, true, kHalfIn, kBfPlanes>(weight, blockIdx.x - left_blocks,
+                                                                  gridDim.x - left_blocks);
   }
 }
 
@@ -301,26 +320,27 @@ __device__ __forceinline__ void store_output_vector(int o, const VecF<VEC>& x, i
   }
 }
 
-template <class Prog, int S, int VEC, bool kHalfOut>
+template <class Prog, int S, int VEC, bool kHalfOut, bool kBfPlanes>
 __device__ __forceinline__ void recombine_vector(const typename VecIO<VEC>::H (&raw)[Prog::kInputs],
                                                  int64_t i, int64_t j, int64_t bm, int64_t bn,
                                                  const uint16_t* __restrict__ bias,
                                                  uint16_t* __restrict__ C, int64_t M, int64_t N,
                                                  int64_t ldc, int vector_stores) {
-  auto in = [&](int r) -> VecF<VEC> { return unpack_half<VEC>(raw[r]); };
+  auto in = [&](int r) -> VecF<VEC> { return unpack_plane<kBfPlanes, VEC>(raw[r]); };
   auto out = [&](int o, const VecF<VEC>& x) {
     store_output_vector<S, VEC, kHalfOut>(o, x, i, j, bm, bn, bias, C, M, N, ldc, vector_stores);
   };
   Prog::template run<VecF<VEC>>(in, out);
 }
 
-// Unfused reconstruct: P[r][bm][ldp] FP16 -> C[M,N].  All R product vectors
-// are loaded before the arithmetic, as in the input side.  The rank-7
-// reconstruct; rank 48/49 use the TMA-staged form (reconstruct_staged.cuh)
-// unless FMM_RECONSTRUCT_VARIANT=register.
-template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false>
+// Unfused reconstruct: P[r][bm][ldp] (FP16, or BF16 with kBfPlanes) -> C[M,N].
+// All R product vectors are loaded before the arithmetic, as in the input
+// side.  The rank-7 reconstruct; rank 48/49 use the TMA-staged form
+// (reconstruct_staged.cuh) unless FMM_RECONSTRUCT_VARIANT=register.
+template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false,
+          bool kBfPlanes = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
-    const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
+    const uint16_t* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
     const uint16_t* __restrict__ bias, uint16_t* __restrict__ C, int64_t M, int64_t N,
     int64_t ldc, int vector_stores) {
   using Raw = typename VecIO<VEC>::H;
@@ -335,7 +355,8 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_kernel(
 #pragma unroll
     for (int r = 0; r < Prog::kInputs; ++r)
       raw[r] = __ldg(reinterpret_cast<const Raw*>(P + r * plane + static_cast<int64_t>(i) * ldp + j));
-    recombine_vector<Prog, S, VEC, kHalfOut>(raw, i, j, bm, bn, bias, C, M, N, ldc, vector_stores);
+    recombine_vector<Prog, S, VEC, kHalfOut, kBfPlanes>(raw, i, j, bm, bn, bias, C, M, N, ldc,
+                                                        vector_stores);
   }
 }
 
@@ -378,9 +399,10 @@ __device__ __forceinline__ void store_output_vector_all(int o, const VecF<VEC>& 
   }
 }
 
-template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false>
+template <class Prog, int S, int VEC, int THREADS = 256, int MIN_BLOCKS = 1, bool kHalfOut = false,
+          bool kBfPlanes = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_gather_kernel(
-    const __half* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
+    const uint16_t* __restrict__ P, int64_t bm, int64_t bn, int64_t ldp,
     const uint16_t* __restrict__ bias, const GatherDests dests, int64_t M, int64_t N, int64_t ldc,
     int vector_stores) {
   using Raw = typename VecIO<VEC>::H;
@@ -395,7 +417,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) reconstruct_gather_kernel
 #pragma unroll
     for (int r = 0; r < Prog::kInputs; ++r)
       raw[r] = __ldg(reinterpret_cast<const Raw*>(P + r * plane + static_cast<int64_t>(i) * ldp + j));
-    auto in = [&](int r) -> VecF<VEC> { return unpack_half<VEC>(raw[r]); };
+    auto in = [&](int r) -> VecF<VEC> { return unpack_plane<kBfPlanes, VEC>(raw[r]); };
     auto out = [&](int o, const VecF<VEC>& x) {
       store_output_vector_all<S, VEC, kHalfOut>(o, x, i, j, bm, bn, bias, dests, M, N, ldc,
                                                 vector_stores);
@@ -426,9 +448,10 @@ struct KnTile {
   static constexpr size_t kBytes = size_t(kQ) * TN * kPitch * 2;
 };
 
-template <class Prog, int S, bool kHalfIn, int TK, int TN, int VEC, int THREADS, int MIN_BLOCKS>
+template <class Prog, int S, bool kHalfIn, int TK, int TN, int VEC, int THREADS, int MIN_BLOCKS,
+          bool kBfPlanes = false>
 __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) right_transform_kn_kernel(
-    const uint16_t* __restrict__ B, int64_t K, int64_t N, int64_t ldb, __half* __restrict__ dst,
+    const uint16_t* __restrict__ B, int64_t K, int64_t N, int64_t ldb, uint16_t* __restrict__ dst,
     int64_t bk, int64_t bn, int64_t ldk, int vector_loads) {
   using T = KnTile<S, TK, TN>;
   static_assert(TN % 8 == 0, "16-byte source chunks");
@@ -477,7 +500,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) right_transform_kn_kernel
       return unpack_in<kHalfIn, VEC>(raw);
     };
     auto out = [&](int o, const VecF<VEC>& x) {
-      store_half_vec<VEC>(dst + o * plane + n * ldk + k, x);
+      store_plane_vec<kBfPlanes, VEC>(dst + o * plane + n * ldk + k, x);
     };
     Prog::template run<VecF<VEC>>(in, out);
   }

@@ -29,6 +29,7 @@ import torch
 FMM_OK = 0
 FMM_DTYPE_BF16 = 0
 FMM_DTYPE_F16 = 1
+FMM_DTYPE_BF16_BF16 = 2
 
 
 class FmmDims(ctypes.Structure):
@@ -57,6 +58,9 @@ ARGTYPES = {
     # int fmm_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn,
     #                   int64_t bk, void* P, fmm_stream_t stream)
     "fmm_leaf_gemm": [_INT, _P, _P, _I64, _I64, _I64, _P, _P],
+    # int fmm_leaf_gemm_bf16(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn,
+    #                        int64_t bk, void* P, fmm_stream_t stream)
+    "fmm_leaf_gemm_bf16": [_INT, _P, _P, _I64, _I64, _I64, _P, _P],
     # int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N,
     #                     const void* bias, void* C, int64_t ldc, fmm_stream_t stream)
     "fmm_reconstruct": [_INT, _INT, _P, _I64, _I64, _P, _P, _I64, _P],
@@ -91,12 +95,17 @@ def _check(rc: int, what: str) -> None:
         raise RuntimeError(f"{what}: {library().fmm_last_error_string().decode()} (error {rc})")
 
 
-def _dtype(tensor: torch.Tensor) -> int:
-    if tensor.dtype == torch.bfloat16:
+def _dtype(tensor: torch.Tensor, planes: torch.Tensor) -> int:
+    """Precision id: the operand (or output) type with the plane type -- the
+    plan's ``(dtype, compute_dtype)`` pair."""
+    pair = (tensor.dtype, planes.dtype)
+    if pair == (torch.bfloat16, torch.float16):
         return FMM_DTYPE_BF16
-    if tensor.dtype == torch.float16:
+    if pair == (torch.float16, torch.float16):
         return FMM_DTYPE_F16
-    raise ValueError(f"libfmm_sm100 takes BF16 or FP16 operands, not {tensor.dtype}")
+    if pair == (torch.bfloat16, torch.bfloat16):
+        return FMM_DTYPE_BF16_BF16
+    raise ValueError(f"libfmm_sm100 does not take {tensor.dtype} operands with {planes.dtype} planes")
 
 
 def _stream(tensor: torch.Tensor) -> int:
@@ -117,27 +126,29 @@ class B200Launches:
 
     def _transform_left(self, source: torch.Tensor, output: torch.Tensor) -> None:
         rows, inner = source.shape
-        _check(library().fmm_transform_a(self.rank, _dtype(source), source.data_ptr(), rows, inner,
+        _check(library().fmm_transform_a(self.rank, _dtype(source, output), source.data_ptr(), rows, inner,
                                          source.stride(0), output.data_ptr(), _stream(source)),
                "fmm_transform_a")
 
     def _transform_right(self, source: torch.Tensor, output: torch.Tensor) -> None:
         inner, columns = source.shape
-        _check(library().fmm_transform_b(self.rank, _dtype(source), source.data_ptr(), inner, columns,
+        _check(library().fmm_transform_b(self.rank, _dtype(source, output), source.data_ptr(), inner, columns,
                                          source.stride(0), output.data_ptr(), _stream(source)),
                "fmm_transform_b")
 
     def _transform_weight(self, source: torch.Tensor, output: torch.Tensor) -> None:
         columns, inner = source.shape
-        _check(library().fmm_transform_w(self.rank, _dtype(source), source.data_ptr(), columns, inner,
+        _check(library().fmm_transform_w(self.rank, _dtype(source, output), source.data_ptr(), columns, inner,
                                          source.stride(0), output.data_ptr(), _stream(source)),
                "fmm_transform_w")
 
     def _products(self, left: torch.Tensor, right: torch.Tensor, products: torch.Tensor) -> None:
-        """Replaces ``torch.bmm(left, right, out=products)``."""
+        """Replaces ``torch.bmm(left, right, out=products)`` (FP16 planes, or
+        BF16 planes for the rank-49 ``(bfloat16, bfloat16)`` pair)."""
         s = self.shape
-        _check(library().fmm_leaf_gemm(self.rank, left.data_ptr(), right.data_ptr(), s.block_rows,
-                                       s.block_columns, s.block_inner, products.data_ptr(), _stream(left)),
+        gemm = library().fmm_leaf_gemm_bf16 if left.dtype == torch.bfloat16 else library().fmm_leaf_gemm
+        _check(gemm(self.rank, left.data_ptr(), right.data_ptr(), s.block_rows, s.block_columns,
+                    s.block_inner, products.data_ptr(), _stream(left)),
                "fmm_leaf_gemm")
 
     def _reconstruct(self, products: torch.Tensor, output: torch.Tensor) -> None:
@@ -146,7 +157,7 @@ class B200Launches:
     def _reconstruct_bias(self, products: torch.Tensor, bias: torch.Tensor | None,
                           output: torch.Tensor) -> None:
         rows, columns = output.shape
-        _check(library().fmm_reconstruct(self.rank, _dtype(output), products.data_ptr(), rows, columns,
+        _check(library().fmm_reconstruct(self.rank, _dtype(output, products), products.data_ptr(), rows, columns,
                                          None if bias is None else bias.data_ptr(), output.data_ptr(),
                                          output.stride(0), _stream(products)),
                "fmm_reconstruct")

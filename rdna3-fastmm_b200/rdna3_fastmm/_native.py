@@ -25,6 +25,7 @@ FMM_LINEAR_PREPACKED = 1
 FMM_RIGHT_KN = 2
 FMM_DTYPE_BF16 = 0
 FMM_DTYPE_F16 = 1
+FMM_DTYPE_BF16_BF16 = 2
 
 SCHEME_IDS = {"rank7": 7, "rank48": 48, "rank49": 49, "rank343": 343}
 
@@ -58,6 +59,7 @@ _SIGNATURES = {
     "fmm_transform_w": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_transform_b": ([ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_leaf_gemm": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
+    "fmm_leaf_gemm_bf16": ([ctypes.c_int, _P, _P, _I64, _I64, _I64, _P, _P], ctypes.c_int),
     "fmm_ipc_export": ([_P, ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
     "fmm_ipc_import": (
         [ctypes.POINTER(ctypes.c_ubyte), ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
@@ -137,25 +139,31 @@ def _stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def dtype_id(dtype) -> int:
+def dtype_id(dtype, plane_dtype=None) -> int:
+    """Precision id of a call: operand/output type ``dtype`` with planes of
+    ``plane_dtype`` (FP16 when omitted)."""
     import torch
 
-    if dtype == torch.bfloat16:
+    plane_dtype = torch.float16 if plane_dtype is None else plane_dtype
+    if dtype == torch.bfloat16 and plane_dtype == torch.float16:
         return FMM_DTYPE_BF16
-    if dtype == torch.float16:
+    if dtype == torch.float16 and plane_dtype == torch.float16:
         return FMM_DTYPE_F16
-    raise ValueError(f"libfmm_sm100 takes BF16 or FP16 operands, not {dtype}")
+    if dtype == torch.bfloat16 and plane_dtype == torch.bfloat16:
+        return FMM_DTYPE_BF16_BF16
+    raise ValueError(f"libfmm_sm100 takes BF16 or FP16 operands with FP16 planes, or BF16 operands "
+                     f"with BF16 planes, not {dtype} with {plane_dtype} planes")
 
 
 def transform_a(scheme: str, A, L) -> None:
     M, K = A.shape
-    check(library().fmm_transform_a(SCHEME_IDS[scheme], dtype_id(A.dtype), _ptr(A), M, K, A.stride(0),
+    check(library().fmm_transform_a(SCHEME_IDS[scheme], dtype_id(A.dtype, L.dtype), _ptr(A), M, K, A.stride(0),
                                     _ptr(L), _stream(A.device)), "fmm_transform_a")
 
 
 def transform_w(scheme: str, W, Rt) -> None:
     N, K = W.shape
-    check(library().fmm_transform_w(SCHEME_IDS[scheme], dtype_id(W.dtype), _ptr(W), N, K, W.stride(0),
+    check(library().fmm_transform_w(SCHEME_IDS[scheme], dtype_id(W.dtype, Rt.dtype), _ptr(W), N, K, W.stride(0),
                                     _ptr(Rt), _stream(W.device)), "fmm_transform_w")
 
 
@@ -163,24 +171,31 @@ def transform_aw(scheme: str, A, L, W, Rt) -> None:
     """Both input-side transforms of a dynamic linear in one launch."""
     M, K = A.shape
     N = W.shape[0]
-    check(library().fmm_transform_aw(SCHEME_IDS[scheme], dtype_id(A.dtype), _ptr(A), M, K, A.stride(0),
+    check(library().fmm_transform_aw(SCHEME_IDS[scheme], dtype_id(A.dtype, L.dtype), _ptr(A), M, K, A.stride(0),
                                      _ptr(L), _ptr(W), N, W.stride(0), _ptr(Rt), _stream(A.device)),
           "fmm_transform_aw")
 
 
 def transform_b(scheme: str, B, Rt) -> None:
     K, N = B.shape
-    check(library().fmm_transform_b(SCHEME_IDS[scheme], dtype_id(B.dtype), _ptr(B), K, N, B.stride(0),
+    check(library().fmm_transform_b(SCHEME_IDS[scheme], dtype_id(B.dtype, Rt.dtype), _ptr(B), K, N, B.stride(0),
                                     _ptr(Rt), _stream(B.device)), "fmm_transform_b")
 
 
 def leaf_gemm(rank: int, L, Rt, bm: int, bn: int, bk: int, P) -> None:
+    """Leaf products on FP16 planes, or on BF16 planes when L is BF16."""
+    import torch
+
+    if L.dtype == torch.bfloat16:
+        check(library().fmm_leaf_gemm_bf16(rank, _ptr(L), _ptr(Rt), bm, bn, bk, _ptr(P), _stream(L.device)),
+              "fmm_leaf_gemm_bf16")
+        return
     check(library().fmm_leaf_gemm(rank, _ptr(L), _ptr(Rt), bm, bn, bk, _ptr(P), _stream(L.device)),
           "fmm_leaf_gemm")
 
 
 def reconstruct(scheme: str, P, M: int, N: int, bias, C) -> None:
-    check(library().fmm_reconstruct(SCHEME_IDS[scheme], dtype_id(C.dtype), _ptr(P), M, N, _ptr(bias),
+    check(library().fmm_reconstruct(SCHEME_IDS[scheme], dtype_id(C.dtype, P.dtype), _ptr(P), M, N, _ptr(bias),
                                     _ptr(C), C.stride(0), _stream(P.device)), "fmm_reconstruct")
 
 
@@ -212,7 +227,8 @@ def reconstruct_gather(scheme: str, P, M: int, N: int, bias, dests: list[int], l
     ``dests`` (device addresses of this rank's first row in the own and the
     peers' gathered outputs, leading dimension ``ldc``)."""
     array = (ctypes.c_void_p * len(dests))(*dests)
-    check(library().fmm_reconstruct_gather(SCHEME_IDS[scheme], dtype_id(dtype), _ptr(P), M, N, _ptr(bias),
+    check(library().fmm_reconstruct_gather(SCHEME_IDS[scheme], dtype_id(dtype, P.dtype), _ptr(P), M, N,
+                                           _ptr(bias),
                                            array, len(dests), ldc, _stream(P.device)),
           "fmm_reconstruct_gather")
 
@@ -223,7 +239,7 @@ def linear(scheme: str, A, W, bias, C, L, Rt, P, prepacked: bool, right_kn: bool
     M, K = A.shape
     N = C.shape[1]
     flags = (FMM_LINEAR_PREPACKED if prepacked else 0) | (FMM_RIGHT_KN if right_kn else 0)
-    check(library().fmm_linear(SCHEME_IDS[scheme], dtype_id(A.dtype), _ptr(A), _ptr(W), _ptr(bias),
+    check(library().fmm_linear(SCHEME_IDS[scheme], dtype_id(A.dtype, L.dtype), _ptr(A), _ptr(W), _ptr(bias),
                                _ptr(C), M, K, N, _ptr(L), _ptr(Rt), _ptr(P), flags, _stream(A.device)),
           "fmm_linear")
 

@@ -522,7 +522,9 @@ class Rank49Plan(_LinearPlan):
     scheme = "rank49"
     rank = 49
     scheme_size = 4
-    precision_pairs = _FP16_AND_BF16_FP16
+    # (bfloat16, bfloat16): BF16 planes, BF16 leaf products (tcgen05 with BF16
+    # operands), as the reference's pair of the same name
+    precision_pairs = _FP16_AND_BF16_FP16 | frozenset({(torch.bfloat16, torch.bfloat16)})
     linear_shape_families: tuple[LinearShapeFamily, ...] = ()
     prepacked_linear_shape_families: tuple[LinearShapeFamily, ...] = ()
 

@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 PLANS = {"rank7": Rank7Plan, "rank48": Rank48Plan, "rank49": Rank49Plan}
 
 
-def make_reference_style_plan(binding, name, M, K, N):
+def make_reference_style_plan(binding, name, M, K, N, planes=torch.float16):
     scheme_size = PLANS[name].scheme_size
 
     class Plan(binding.B200Launches):
@@ -31,7 +31,7 @@ def make_reference_style_plan(binding, name, M, K, N):
 
         def workspace(self, device, prepacked: bool):
             shapes = binding.plane_shapes(self.rank, M, K, N)
-            return {k: torch.empty(v, device=device, dtype=torch.float16) for k, v in shapes.items()
+            return {k: torch.empty(v, device=device, dtype=planes) for k, v in shapes.items()
                     if not (prepacked and k == "right")}
 
         def run_linear(self, x, weight, ws, bias, out):  # runtime.py:700-741
@@ -87,3 +87,25 @@ def test_reference_launch_sequence_through_the_binding(name, shape, with_bias):
     expected = own.run_linear(Ad, Wd, own.allocate_workspace(0.5), bd)
     torch.cuda.synchronize(device)
     assert torch.equal(out.view(torch.int16), expected.view(torch.int16))
+
+
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_reference_launch_sequence_with_bf16_planes(with_bias):
+    """Rank49Plan's (bfloat16, bfloat16) pair through the binding: BF16 planes
+    and products, the BF16 leaf GEMM entry point."""
+    binding = load_binding()
+    binding._lib = binding.load(str(_native.LIBRARY_PATH))
+    M, K, N = 257, 263, 269
+    device = torch.device("cuda", 0)
+    A, W, bias = make_linear_inputs(M, K, N, seed=0, bias=with_bias)
+    Ad, Wd = A.to(device), W.to(device)
+    bd = bias.to(device) if bias is not None else None
+    plan = make_reference_style_plan(binding, "rank49", M, K, N, planes=torch.bfloat16)
+    out = torch.empty((M, N), device=device, dtype=torch.bfloat16)
+    plan.run_linear(Ad, Wd, plan.workspace(device, False), bd, out)
+    own = Rank49Plan(M, K, N, device, dtype=torch.bfloat16, compute_dtype=torch.bfloat16)
+    expected = own.run_linear(Ad, Wd, own.allocate_workspace(0.5), bd)
+    torch.cuda.synchronize(device)
+    assert torch.equal(out.view(torch.int16), expected.view(torch.int16))
+    ref = oracle.linear("rank49", f32(A), f32(W), f32(bias) if bias is not None else None, planes="bf16")
+    assert oracle.relative_l2(out.float().cpu().numpy(), ref) < 2e-3

@@ -81,7 +81,7 @@ def test_plan_rejects_cpu_device(plan):
         plan(4, 4, 4, torch.device("cpu"))
 
 
-@pytest.mark.parametrize("plan", [Rank7Plan, Rank48Plan, Rank49Plan])
+@pytest.mark.parametrize("plan", [Rank7Plan, Rank48Plan])
 def test_plan_rejects_unsupported_precision(monkeypatch, plan):
     configure_supported_runtime(monkeypatch)
     with pytest.raises(ValueError, match="does not support"):
@@ -92,13 +92,25 @@ def test_plan_rejects_unsupported_precision(monkeypatch, plan):
 
 def test_precision_pairs_follow_the_reference(monkeypatch):
     """FP16 plans exist for rank 7 and rank 49 (reference runtime.py:785-790,
-    852-858); rank 48 is BF16-in only (:828)."""
+    852-858); rank 48 is BF16-in only (:828); only rank 49 has BF16 planes
+    (:855), and a BF16 rank-49 plan without compute_dtype resolves to them."""
     configure_supported_runtime(monkeypatch)
+    dev = torch.device("cuda", 0)
     for plan in (Rank7Plan, Rank49Plan):
-        p = plan(4, 4, 4, torch.device("cuda", 0))  # default dtype FP16
+        p = plan(4, 4, 4, dev)  # default dtype FP16
         assert (p.dtype, p.compute_dtype) == (torch.float16, torch.float16)
     with pytest.raises(ValueError, match="does not support"):
-        Rank48Plan(4, 4, 4, torch.device("cuda", 0))
+        Rank48Plan(4, 4, 4, dev)
+    p = Rank49Plan(4, 4, 4, dev, dtype=torch.bfloat16)
+    assert (p.dtype, p.compute_dtype) == (torch.bfloat16, torch.bfloat16)
+    assert p.packed_weight_bytes == Rank49Plan(4, 4, 4, dev, dtype=torch.bfloat16,
+                                               compute_dtype=torch.float16).packed_weight_bytes
+    assert not p.is_linear_recommended(has_bias=False)
+    with pytest.raises(ValueError, match="does not support"):
+        Rank49Plan(4, 4, 4, dev, dtype=torch.float32)
+    assert Rank49Plan.precision_pairs == frozenset({(torch.float16, torch.float16),
+                                                    (torch.bfloat16, torch.bfloat16),
+                                                    (torch.bfloat16, torch.float16)})
 
 
 def test_mm_tables_hold_only_measured_b200_wins():
