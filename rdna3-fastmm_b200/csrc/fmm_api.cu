@@ -509,6 +509,10 @@ using PairCfg256 = LeafGemmPairConfig<256, 7>;
 using PairCfg192 = LeafGemmPairConfig<192, 7>;
 using PairCfg128 = LeafGemmPairConfig<128, 8>;
 using PairCfg256K128 = LeafGemmPairConfig<256, 3, 128>;
+// the same two tiles with the TMA-store epilogue (one stage fewer for the
+// epilogue's 16 KiB of shared-memory store buffers)
+using PairCfg256Tma = LeafGemmPairConfig<256, 6, 64, true>;
+using PairCfg256K128Tma = LeafGemmPairConfig<256, 3, 128, true>;
 
 enum GemmVariant {
   kVariantSingle = 0,
@@ -563,6 +567,13 @@ int choose_variant(int64_t rank, int64_t bm, int64_t bn, int sms) {
   return best;
 }
 
+// Epilogue of the 256 x 256 pair GEMM: FMM_LEAF_GEMM_EPILOGUE=rows keeps the
+// per-lane row stores, =tma the shared-memory staged TMA stores.
+bool tma_store_epilogue() {
+  const char* v = std::getenv("FMM_LEAF_GEMM_EPILOGUE");
+  return v != nullptr && std::string(v) == "tma";
+}
+
 template <class Kernel>
 int ensure_smem_attribute(bool& done, Kernel kernel, size_t bytes) {
   if (done) return FMM_OK;
@@ -586,6 +597,14 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, Cfg::kBN / 2)) return rc;
   // 16-row boxes for the ragged last N tile's halves
   if (int rc = plane_map(&map_r16, Rt, prm.bk, prm.bn, ldk, prm.rank, 16)) return rc;
+  // P[rank][bm][ldp] for the TMA-store epilogue: boxes of 32 columns x 32 rows,
+  // 64-byte swizzle (unused by the row-store epilogue)
+  CUtensorMap map_p = map_l;
+  if constexpr (Cfg::kTmaStore) {
+    if (int rc = tiled_map_3d(&map_p, prm.P, {prm.ldp, prm.bm, int64_t(prm.rank)},
+                              {prm.ldp * 2, prm.bm * prm.ldp * 2}, {32u, 32u, 1u}, CU_TENSOR_MAP_SWIZZLE_64B))
+      return rc;
+  }
   {
     std::lock_guard<std::mutex> lock(g_device_mutex);
     if (int rc = ensure_smem_attribute(configured[dev], leaf_gemm_pair_kernel<Cfg, kBf16>, Cfg::kSmemBytes))
@@ -605,7 +624,7 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg, kBf16>, map_l, map_r, map_r16, prm);
+  e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg, kBf16>, map_l, map_r, map_r16, map_p, prm);
   if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM (pair) launch");
   return FMM_OK;
 }
@@ -782,13 +801,18 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   const int sms = usable_sms(info);
   int variant = choose_variant(rank, bm, bn, sms);
   if (kBf16 && (variant == kVariantPair192 || variant == kVariantPair128)) variant = kVariantPair256;
+  const bool tma_store = tma_store_epilogue();
+  if (variant == kVariantPair256 && bk >= 3072) variant = kVariantPair256K128;
   if (variant == kVariantPair256) {
+    return tma_store ? launch_pair<PairCfg256Tma, kBf16>(L, Rt, prm, ldk, sms, stream)
+                     : launch_pair<PairCfg256, kBf16>(L, Rt, prm, ldk, sms, stream);
+  }
+  if (variant == kVariantPair256K128) {
     // deep leaves: 128-deep k-blocks in 3 stages (half the barrier round trips per
     // FLOP) measured 0.3-2.8 % faster from bk = 3072 up and 1-3 % slower below
-    if (bk >= 3072) return launch_pair<PairCfg256K128, kBf16>(L, Rt, prm, ldk, sms, stream);
-    return launch_pair<PairCfg256, kBf16>(L, Rt, prm, ldk, sms, stream);
+    return tma_store ? launch_pair<PairCfg256K128Tma, kBf16>(L, Rt, prm, ldk, sms, stream)
+                     : launch_pair<PairCfg256K128, kBf16>(L, Rt, prm, ldk, sms, stream);
   }
-  if (variant == kVariantPair256K128) return launch_pair<PairCfg256K128, kBf16>(L, Rt, prm, ldk, sms, stream);
   if constexpr (!kBf16) {
     if (variant == kVariantPair192) return launch_pair<PairCfg192, false>(L, Rt, prm, ldk, sms, stream);
     if (variant == kVariantPair128) return launch_pair<PairCfg128, false>(L, Rt, prm, ldk, sms, stream);

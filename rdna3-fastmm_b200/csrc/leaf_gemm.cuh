@@ -309,10 +309,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // No TMA multicast is used: every CTA loads only its own halves.  Deep leaves
 // (bk >= 3072) use 128-deep k-blocks in 3 stages: two 64-deep atom columns per
 // operand and stage, half the barrier round trips per FLOP.
-template <int BN, int STAGES, int BK = kGemmBK>
+template <int BN, int STAGES, int BK = kGemmBK, bool TMA_STORE = false>
 struct LeafGemmPairConfig {
   static constexpr int kBN = BN;
   static constexpr int kStages = STAGES;
+  // Epilogue: per-lane 16-byte row stores (false), or each warp stages 32 x 32
+  // FP16 blocks in shared memory (64-byte swizzle, two buffers a warp) and
+  // writes them with TMA stores (true)
+  static constexpr bool kTmaStore = TMA_STORE;
+  static constexpr uint32_t kStoreBufBytes = 32 * 32 * 2;
+  static constexpr uint32_t kStoreBytes = TMA_STORE ? 4 * 2 * kStoreBufBytes : 0;
   // k-block depth 64 or 128: one or two 64-deep columns of 128-byte swizzle
   // atoms per operand and stage
   static constexpr int kBK = BK;
@@ -326,9 +332,10 @@ struct LeafGemmPairConfig {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   // two accumulators of BN columns; the allocation is a power of two
   static constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256 : 512;
-  // stages + 1 KiB slack for the 1024-byte alignment + the barrier block
-  // (2 * STAGES + 5 barriers, the TMEM slot and the abort flag)
-  static constexpr size_t kSmemBytes = size_t(STAGES) * kStageBytes + 1024 + 8 * (2 * STAGES + 8);
+  // stages + store buffers + 1 KiB slack for the 1024-byte alignment + the
+  // barrier block (2 * STAGES + 5 barriers, the TMEM slot and the abort flag)
+  static constexpr size_t kSmemBytes =
+      size_t(STAGES) * kStageBytes + kStoreBytes + 1024 + 8 * (2 * STAGES + 8);
   static_assert(2 * BN <= 512 && BN % 32 == 0, "two BN-column accumulators must fit in TMEM");
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
   static_assert(BK == 64 || BK == 128, "k-block depth");
@@ -338,7 +345,8 @@ template <class Cfg, bool kBf16 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     leaf_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_l,
                           const __grid_constant__ CUtensorMap tmap_r,
-                          const __grid_constant__ CUtensorMap tmap_r16, const LeafGemmParams p) {
+                          const __grid_constant__ CUtensorMap tmap_r16,
+                          const __grid_constant__ CUtensorMap tmap_p, const LeafGemmParams p) {
   constexpr int BN = Cfg::kBN;
   constexpr int STAGES = Cfg::kStages;
   constexpr int BK = Cfg::kBK;
@@ -348,7 +356,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + (base - raw_addr);
   const uint32_t a_base = base;
   const uint32_t b_base = base + STAGES * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes);
+  const uint32_t store_base = base + STAGES * Cfg::kStageBytes;  // kTmaStore: 8 buffers of 2 KiB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes + Cfg::kStoreBytes);
   const uint32_t full_bar = smem_u32(bars);                     // [STAGES], used in CTA 0
   const uint32_t empty_bar = smem_u32(bars + STAGES);           // [STAGES], each CTA
   const uint32_t tfull_bar = smem_u32(bars + 2 * STAGES);       // [2], each CTA
@@ -378,6 +387,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tmap_l);
     prefetch_tmap(&tmap_r);
     prefetch_tmap(&tmap_r16);
+    if constexpr (Cfg::kTmaStore) prefetch_tmap(&tmap_p);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -517,6 +527,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tempty_even = map_to_cta(tempty_bar, 0);
     int acc = 0;
     uint32_t acc_phase = 0;
+    int chunk = 0;  // kTmaStore: running count of this warp's staged blocks (buffer = chunk & 1)
     for (int t = pair; t < total_tiles; t += pairs) {
       int r, tm, tn;
       leaf_tile_coords(q, t, r, tm, tn);
@@ -537,18 +548,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_ld_32x32b_x32(t_addr + c, v);
         tc_wait_ld();
         const int64_t col = static_cast<int64_t>(tn) * BN + c;
-        if (row < p.bm) {
+        if constexpr (Cfg::kTmaStore) {
+          // this lane's row of a 32 x 32 FP16 block, 64-byte swizzled: 16-byte
+          // chunk j of row l sits at l * 64 + ((j ^ ((l >> 1) & 3)) << 4), the
+          // layout a SWIZZLE_64B tensor map reads (and conflict-free per 8 lanes)
+          uint32_t w[16];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int64_t c8 = col + g * 8;
-            if (c8 + 8 <= p.ldp) {
-              uint4 pk;
-              uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+          for (int e = 0; e < 16; ++e)
+            w[e] = pack2_rn<kBf16>(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+          const uint32_t buf = store_base + static_cast<uint32_t>((quarter * 2 + (chunk & 1)) * Cfg::kStoreBufBytes);
+          // the store issued from this buffer two blocks ago must have read it
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                w[e] = pack2_rn<kBf16>(__uint_as_float(v[g * 8 + 2 * e]),
-                                       __uint_as_float(v[g * 8 + 2 * e + 1]));
-              *reinterpret_cast<uint4*>(prow + c8) = pk;
+          for (int j = 0; j < 4; ++j)
+            st_shared_v4(buf + static_cast<uint32_t>(lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)), w[4 * j],
+                         w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          // rows past bm and columns past ldp fall outside the tensor map and are
+          // not written; a block that lies wholly outside is not issued at all
+          const int64_t row0 = static_cast<int64_t>(tm) * Cfg::kTileM + static_cast<int>(cta) * kGemmBM +
+                               quarter * 32;
+          if (lane == 0 && row0 < p.bm && col < p.ldp) {
+            tma_store_3d(&tmap_p, buf, static_cast<int32_t>(col), static_cast<int32_t>(row0), r);
+            bulk_commit_group();
+          }
+          ++chunk;
+        } else {
+          if (row < p.bm) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int64_t c8 = col + g * 8;
+              if (c8 + 8 <= p.ldp) {
+                uint4 pk;
+                uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  w[e] = pack2_rn<kBf16>(__uint_as_float(v[g * 8 + 2 * e]),
+                                         __uint_as_float(v[g * 8 + 2 * e + 1]));
+                *reinterpret_cast<uint4*>(prow + c8) = pk;
+              }
             }
           }
         }
@@ -560,6 +600,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    // the staged blocks' stores must finish (reading shared memory and writing
+    // P) before the CTA leaves
+    if constexpr (Cfg::kTmaStore) {
+      if (lane == 0) bulk_wait_group_all();
+      __syncwarp();
     }
   }
 

@@ -91,13 +91,15 @@ def test_bf16_reconstruct_matches_oracle_bitwise(shape, with_bias, variant, monk
     np.testing.assert_array_equal(_bits(C), _oracle_bits(ref))
 
 
-@pytest.mark.parametrize("variant", ["single", "pair256", "pair256k128"])
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair256k128", "pair256-tma", "pair256k128-tma"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
     [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (49, 64, 72, 130), (5, 700, 900, 520)],
 )
 def test_bf16_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch):
+    variant, _, epilogue = variant.partition("-")
     monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
+    monkeypatch.setenv("FMM_LEAF_GEMM_EPILOGUE", epilogue or "rows")
     g = torch.Generator().manual_seed(rank * 1000 + bm)
     ldk = -(-bk // 8) * 8
     ldp = -(-bn // 8) * 8

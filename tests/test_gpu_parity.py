@@ -139,7 +139,8 @@ def test_reconstruct_unaligned_bias_matches_aligned(name, variant, monkeypatch):
     np.testing.assert_array_equal(_bits(C1), oracle.bf16_bits(ref).view(np.int16))
 
 
-@pytest.mark.parametrize("variant", ["single", "pair256", "pair192", "pair128", "pair256k128"])
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair192", "pair128", "pair256k128",
+                                     "pair256-tma", "pair256k128-tma"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
     [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (2, 129, 257, 1000), (48, 64, 72, 130),
@@ -147,8 +148,11 @@ def test_reconstruct_unaligned_bias_matches_aligned(name, variant, monkeypatch):
 )
 def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch):
     """Every leaf-GEMM kernel (1-SM 128x256; 2-SM 256x256, 256x192, 256x128 with 64-deep
-    k-blocks; 2-SM 256x256 with 128-deep k-blocks)."""
+    k-blocks; 2-SM 256x256 with 128-deep k-blocks), the 256x256 pairs with both
+    epilogues (per-lane row stores; shared-memory staged TMA stores)."""
+    variant, _, epilogue = variant.partition("-")
     monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
+    monkeypatch.setenv("FMM_LEAF_GEMM_EPILOGUE", epilogue or "rows")
     g = torch.Generator().manual_seed(rank * 1000 + bm)
     ldk = -(-bk // 8) * 8
     ldp = -(-bn // 8) * 8
@@ -160,9 +164,12 @@ def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch)
     if ldk > bk:
         L[:, :, bk:] = float("nan")
         Rt[:, :, bk:] = float("nan")
-    P = torch.full((rank, bm, ldp), float("nan"), device="cuda", dtype=torch.float16)
+    # one guard row past the planes: no store may land beyond P
+    P_all = torch.full((rank * bm * ldp + ldp,), float("nan"), device="cuda", dtype=torch.float16)
+    P = P_all[: rank * bm * ldp].view(rank, bm, ldp)
     _native.leaf_gemm(rank, L.cuda(), Rt.cuda(), bm, bn, bk, P)
     torch.cuda.synchronize()
+    assert torch.isnan(P_all[rank * bm * ldp:]).all()
     a, b = L[:, :, :bk].double(), Rt[:, :, :bk].double().transpose(1, 2)
     exact = torch.matmul(a, b)
     magnitude = torch.matmul(a.abs(), b.abs())
