@@ -134,6 +134,7 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.samples: list[tuple[int, int]] = []
+        self.power_mw: list[int] = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._thread = None
@@ -153,6 +154,10 @@ class ClockSampler:
                 while not self._stop.is_set():
                     self.samples.append((pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM),
                                          reasons(handle)))
+                    try:
+                        self.power_mw.append(pynvml.nvmlDeviceGetPowerUsage(handle))
+                    except Exception:  # power readings unsupported: clocks only
+                        pass
                     time.sleep(0.002)
 
             self._thread = threading.Thread(target=poll, daemon=True)
@@ -174,7 +179,11 @@ class ClockSampler:
                 if mask & bit:
                     reasons.add(name)
         out = {"sm_mhz": statistics.median(clocks) if clocks else None, "sm_max_mhz": self.max_mhz,
+               "sm_mhz_min": min(clocks) if clocks else None,
                "reasons": sorted(reasons), "samples": len(clocks), "source": "nvml"}
+        if self.power_mw:
+            out["power_w_median"] = round(statistics.median(self.power_mw) / 1000, 1)
+            out["power_w_max"] = round(max(self.power_mw) / 1000, 1)
         if self.error:
             out["error"] = self.error
         return out
