@@ -466,16 +466,19 @@ int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* out) {
   return FMM_OK;
 }
 
-// Stacked FP16 planes [batch][rows][pitch] as a 3-D map over (k, row, batch);
-// box = 64 K-elements (128 B, swizzled) x box_rows rows x 1 plane.
+// Stacked 16-bit planes [batch][plane_rows][pitch] as a 3-D map over (k, row,
+// batch), covering the first `rows` rows of every plane (rows <= plane_rows;
+// `base` may point into a plane to start the band further down); box = 64
+// K-elements (128 B, swizzled) x box_rows rows x 1 plane.  TMA copies the
+// 2-byte elements without conversion, so the FP16 map serves BF16 planes too.
 int plane_map(CUtensorMap* map, const void* base, int64_t k, int64_t rows, int64_t pitch,
-              int64_t batch, uint32_t box_rows) {
+              int64_t batch, uint32_t box_rows, int64_t plane_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (int rc = tensor_map_encoder(&encode)) return rc;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows),
                         static_cast<cuuint64_t>(batch)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch * 2),
-                           static_cast<cuuint64_t>(pitch * 2 * rows)};
+                           static_cast<cuuint64_t>(pitch * 2 * plane_rows)};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(kGemmBK), box_rows, 1};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
@@ -567,11 +570,20 @@ int choose_variant(int64_t rank, int64_t bm, int64_t bn, int sms) {
   return best;
 }
 
-// Epilogue of the 256 x 256 pair GEMM: FMM_LEAF_GEMM_EPILOGUE=rows keeps the
-// per-lane row stores, =tma the shared-memory staged TMA stores.
-bool tma_store_epilogue() {
-  const char* v = std::getenv("FMM_LEAF_GEMM_EPILOGUE");
-  return v != nullptr && std::string(v) == "tma";
+// Epilogue of the 256 x 256 pair GEMM: per-lane row stores, or shared-memory
+// staged TMA stores (16 KiB of buffers, which costs the 64-deep configuration
+// one of its 7 stages).  Measured on B200 (GEMM alone, full clock, L2 flushed):
+// the TMA stores win where the epilogue of one tile is long against the main
+// loop of the next -- short leaves (c5b, bk = 1152: +8 %) -- and wherever the
+// stage count does not change (128-deep k-blocks, bk >= 3072: c4 +2.5 %, c3
+// +1 %); at bk = 2048 the seventh stage is worth more (c2 -3 %, c5a +-3 %).
+// FMM_LEAF_GEMM_EPILOGUE=rows|tma forces one.
+bool tma_store_epilogue(int64_t bk) {
+  if (const char* v = std::getenv("FMM_LEAF_GEMM_EPILOGUE")) {
+    if (std::string(v) == "tma") return true;
+    if (std::string(v) == "rows") return false;
+  }
+  return bk >= 3072 || bk < 2048;
 }
 
 template <class Kernel>
@@ -593,16 +605,17 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
   CUtensorMap map_l, map_r, map_r16;
-  if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM)) return rc;
-  if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, Cfg::kBN / 2)) return rc;
+  if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM, prm.plane_rows)) return rc;
+  if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, Cfg::kBN / 2, prm.bn)) return rc;
   // 16-row boxes for the ragged last N tile's halves
-  if (int rc = plane_map(&map_r16, Rt, prm.bk, prm.bn, ldk, prm.rank, 16)) return rc;
+  if (int rc = plane_map(&map_r16, Rt, prm.bk, prm.bn, ldk, prm.rank, 16, prm.bn)) return rc;
   // P[rank][bm][ldp] for the TMA-store epilogue: boxes of 32 columns x 32 rows,
   // 64-byte swizzle (unused by the row-store epilogue)
   CUtensorMap map_p = map_l;
   if constexpr (Cfg::kTmaStore) {
     if (int rc = tiled_map_3d(&map_p, prm.P, {prm.ldp, prm.bm, int64_t(prm.rank)},
-                              {prm.ldp * 2, prm.bm * prm.ldp * 2}, {32u, 32u, 1u}, CU_TENSOR_MAP_SWIZZLE_64B))
+                              {prm.ldp * 2, prm.plane_rows * prm.ldp * 2}, {32u, 32u, 1u},
+                              CU_TENSOR_MAP_SWIZZLE_64B))
       return rc;
   }
   {
@@ -756,8 +769,8 @@ int launch_single(const void* L, const void* Rt, const LeafGemmParams& prm, int6
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
   CUtensorMap map_l, map_r;
-  if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM)) return rc;
-  if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, GemmCfg::kBN)) return rc;
+  if (int rc = plane_map(&map_l, L, prm.bk, prm.bm, ldk, prm.rank, kGemmBM, prm.plane_rows)) return rc;
+  if (int rc = plane_map(&map_r, Rt, prm.bk, prm.bn, ldk, prm.rank, GemmCfg::kBN, prm.bn)) return rc;
   {
     std::lock_guard<std::mutex> lock(g_device_mutex);
     if (int rc = ensure_smem_attribute(configured[dev], leaf_gemm_kernel<GemmCfg, kBf16>, GemmCfg::kSmemBytes))
@@ -769,6 +782,62 @@ int launch_single(const void* L, const void* Rt, const LeafGemmParams& prm, int6
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM launch");
   return FMM_OK;
+}
+
+// One GEMM launch over rows [row0, row0 + rows) of every plane (planes of
+// `plane_rows` rows), with the given variant and epilogue.
+template <bool kBf16>
+int launch_leaf_band(int variant, bool tma_store, int rank, const uint16_t* L, const void* Rt,
+                     int64_t row0, int64_t rows, int64_t plane_rows, int64_t bn, int64_t bk,
+                     uint16_t* P, int sms, cudaStream_t stream) {
+  const int64_t ldk = round_up(bk, 8), ldp = round_up(bn, 8);
+  const uint16_t* band_l = L + row0 * ldk;
+  LeafGemmParams prm;
+  prm.bm = rows;
+  prm.bn = bn;
+  prm.bk = bk;
+  prm.ldp = ldp;
+  prm.plane_rows = plane_rows;
+  prm.rank = rank;
+  prm.tiles_m = static_cast<int32_t>(ceil_div(rows, kGemmBM));
+  prm.tiles_n = static_cast<int32_t>(ceil_div(bn, GemmCfg::kBN));
+  prm.group_m = 16;
+  prm.P = P + row0 * ldp;
+  prm.timeout_ns = g_timeout_ns;
+  if (variant == kVariantPair256) {
+    return tma_store ? launch_pair<PairCfg256Tma, kBf16>(band_l, Rt, prm, ldk, sms, stream)
+                     : launch_pair<PairCfg256, kBf16>(band_l, Rt, prm, ldk, sms, stream);
+  }
+  if (variant == kVariantPair256K128) {
+    return tma_store ? launch_pair<PairCfg256K128Tma, kBf16>(band_l, Rt, prm, ldk, sms, stream)
+                     : launch_pair<PairCfg256K128, kBf16>(band_l, Rt, prm, ldk, sms, stream);
+  }
+  if constexpr (!kBf16) {
+    if (variant == kVariantPair192) return launch_pair<PairCfg192, false>(band_l, Rt, prm, ldk, sms, stream);
+    if (variant == kVariantPair128) return launch_pair<PairCfg128, false>(band_l, Rt, prm, ldk, sms, stream);
+  }
+  return launch_single<kBf16>(band_l, Rt, prm, ldk, sms, stream);
+}
+
+// Rows of a short last M tile of the 2-SM GEMM: when the planes' last 256-row
+// tile holds at most 128 rows (c4: bm = 2054, 6 rows), those rows go to a
+// second, 1-SM launch of 128-row tiles, which spends one SM instead of two
+// on each of them; used when the cost model counts fewer tile waves for the
+// two launches together.  FMM_LEAF_GEMM_TAIL=0 keeps one launch, =1 splits
+// whenever the last tile qualifies.
+int64_t split_tail_rows(int variant, int64_t rank, int64_t bm, int64_t bn, int sms) {
+  if (variant == kVariantSingle) return 0;
+  const int64_t tail = bm % 256;
+  if (bm < 256 || tail == 0 || tail > 128) return 0;
+  if (const char* v = std::getenv("FMM_LEAF_GEMM_TAIL")) {
+    if (std::string(v) == "0") return 0;
+    if (std::string(v) == "1") return tail;
+  }
+  const int cost_variant = variant == kVariantPair256K128 ? int(kVariantPair256) : variant;
+  const double whole = variant_cost(cost_variant, rank, bm, bn, sms);
+  const double split = variant_cost(cost_variant, rank, bm - tail, bn, sms) +
+                       variant_cost(kVariantSingle, rank, tail, bn, sms);
+  return split < whole ? tail : 0;
 }
 
 // FP16 planes (kBf16 = false) or BF16 planes.  The BF16 form carries the
@@ -784,40 +853,25 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
     return fail(FMM_ERR_MISALIGNED, "leaf GEMM planes must be 16-byte aligned");
   DeviceInfo* info = nullptr;
   if (int rc = device_info(&info)) return rc;
-  const int64_t ldk = round_up(bk, 8), ldp = round_up(bn, 8);
-  LeafGemmParams prm;
-  prm.bm = bm;
-  prm.bn = bn;
-  prm.bk = bk;
-  prm.ldp = ldp;
-  prm.rank = rank;
-  prm.tiles_m = static_cast<int32_t>(ceil_div(bm, kGemmBM));
-  prm.tiles_n = static_cast<int32_t>(ceil_div(bn, GemmCfg::kBN));
-  prm.group_m = 16;
-  prm.P = static_cast<uint16_t*>(P);
-  prm.timeout_ns = g_timeout_ns;
   if (int64_t(rank) * ceil_div(bm, kGemmBM) * ceil_div(bn, 128) > (int64_t(1) << 30))
     return fail(FMM_ERR_TOO_LARGE, "too many GEMM tiles");
   const int sms = usable_sms(info);
   int variant = choose_variant(rank, bm, bn, sms);
   if (kBf16 && (variant == kVariantPair192 || variant == kVariantPair128)) variant = kVariantPair256;
-  const bool tma_store = tma_store_epilogue();
+  const bool tma_store = tma_store_epilogue(bk);
+  // deep leaves: 128-deep k-blocks in 3 stages (half the barrier round trips per
+  // FLOP) measured 0.3-2.8 % faster from bk = 3072 up and 1-3 % slower below
   if (variant == kVariantPair256 && bk >= 3072) variant = kVariantPair256K128;
-  if (variant == kVariantPair256) {
-    return tma_store ? launch_pair<PairCfg256Tma, kBf16>(L, Rt, prm, ldk, sms, stream)
-                     : launch_pair<PairCfg256, kBf16>(L, Rt, prm, ldk, sms, stream);
-  }
-  if (variant == kVariantPair256K128) {
-    // deep leaves: 128-deep k-blocks in 3 stages (half the barrier round trips per
-    // FLOP) measured 0.3-2.8 % faster from bk = 3072 up and 1-3 % slower below
-    return tma_store ? launch_pair<PairCfg256K128Tma, kBf16>(L, Rt, prm, ldk, sms, stream)
-                     : launch_pair<PairCfg256K128, kBf16>(L, Rt, prm, ldk, sms, stream);
-  }
-  if constexpr (!kBf16) {
-    if (variant == kVariantPair192) return launch_pair<PairCfg192, false>(L, Rt, prm, ldk, sms, stream);
-    if (variant == kVariantPair128) return launch_pair<PairCfg128, false>(L, Rt, prm, ldk, sms, stream);
-  }
-  return launch_single<kBf16>(L, Rt, prm, ldk, sms, stream);
+  const uint16_t* l16 = static_cast<const uint16_t*>(L);
+  uint16_t* p16 = static_cast<uint16_t*>(P);
+  const int64_t tail = split_tail_rows(variant, rank, bm, bn, sms);
+  if (int rc = launch_leaf_band<kBf16>(variant, tma_store, rank, l16, Rt, 0, bm - tail, bm, bn, bk, p16, sms,
+                                       stream))
+    return rc;
+  if (tail == 0) return FMM_OK;
+  // the short last band: same stream, after the 2-SM launch
+  return launch_leaf_band<kBf16>(kVariantSingle, false, rank, l16, Rt, bm - tail, tail, bm, bn, bk, p16, sms,
+                                 stream);
 }
 
 // Device address of g_noalloc_scratch on the current device.  In host code the

@@ -44,6 +44,9 @@ struct LeafGemmConfig {
 struct LeafGemmParams {
   int64_t bm, bn, bk;
   int64_t ldp;
+  // rows between consecutive planes of L and P (>= bm): bm for a whole
+  // launch, the full plane height when a launch covers a band of rows
+  int64_t plane_rows;
   int32_t rank;
   int32_t tiles_m, tiles_n;
   int32_t group_m;
@@ -244,7 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ready) break;
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tm) * kGemmBM + row_in_tile;
-      uint16_t* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
+      uint16_t* prow = p.P + (static_cast<int64_t>(r) * p.plane_rows + row) * p.ldp;
       const uint32_t t_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int n_cols = tile_n_columns(p, tn, BN, 16);
@@ -538,7 +541,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ready) break;
       tc_fence_after();
       const int64_t row = static_cast<int64_t>(tm) * Cfg::kTileM + row_in_tile;
-      uint16_t* prow = p.P + (static_cast<int64_t>(r) * p.bm + row) * p.ldp;
+      uint16_t* prow = p.P + (static_cast<int64_t>(r) * p.plane_rows + row) * p.ldp;
       const uint32_t t_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int n_cols = tile_n_columns(q, tn, BN, 32);

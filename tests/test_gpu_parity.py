@@ -182,6 +182,40 @@ def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch)
     assert torch.all((got - exact).abs() <= bound)
 
 
+@pytest.mark.parametrize("variant", ["pair256", "pair256k128"])
+@pytest.mark.parametrize("rank,bm,bn,bk", [(3, 262, 300, 200), (2, 517, 260, 136), (48, 2054, 72, 64)])
+def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, monkeypatch):
+    """A short last M band (bm % 256 <= 128) run as a second, 1-SM launch over
+    the planes' last rows (FMM_LEAF_GEMM_TAIL=1 forces the split): the rows of
+    the 2-SM band equal the single-launch products bit for bit, the band's rows
+    stay within the product bound of an FP64 product, and nothing outside the
+    planes is written."""
+    monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
+    g = torch.Generator().manual_seed(bm)
+    ldk, ldp = -(-bk // 8) * 8, -(-bn // 8) * 8
+    L = torch.zeros((rank, bm, ldk), dtype=torch.float16)
+    Rt = torch.zeros((rank, bn, ldk), dtype=torch.float16)
+    L[:, :, :bk] = torch.randn((rank, bm, bk), generator=g).half()
+    Rt[:, :, :bk] = torch.randn((rank, bn, bk), generator=g).half()
+    L, Rt = L.cuda(), Rt.cuda()
+    outs = []
+    for tail in ("0", "1"):
+        monkeypatch.setenv("FMM_LEAF_GEMM_TAIL", tail)
+        P_all = torch.full((rank * bm * ldp + ldp,), float("nan"), device="cuda", dtype=torch.float16)
+        P = P_all[: rank * bm * ldp].view(rank, bm, ldp)
+        _native.leaf_gemm(rank, L, Rt, bm, bn, bk, P)
+        torch.cuda.synchronize()
+        assert torch.isnan(P_all[rank * bm * ldp:]).all()
+        assert torch.isfinite(P[:, :, :bn]).all()
+        outs.append(P[:, :, :bn].clone())
+    main = bm - bm % 256
+    assert torch.equal(outs[0][:, :main].view(torch.int16), outs[1][:, :main].view(torch.int16))
+    a, b = L[:, main:, :bk].double().cpu(), Rt[:, :, :bk].double().cpu().transpose(1, 2)
+    exact = torch.matmul(a, b)
+    bound = torch.clamp(exact.abs(), min=2.0**-14) * 2.0**-10 + (bk + 2) * 2.0**-23 * torch.matmul(a.abs(), b.abs())
+    assert torch.all((outs[1][:, main:].cpu().double() - exact).abs() <= bound)
+
+
 @pytest.mark.parametrize("name", list(PLANS))
 @pytest.mark.parametrize("shape", [(5, 6, 7), (257, 263, 269), (512, 1024, 1024)],
                          ids=lambda s: "x".join(map(str, s)))
