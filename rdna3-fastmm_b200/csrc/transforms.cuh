@@ -16,39 +16,126 @@ struct VecF {
   float v[N];
 };
 
-// One FP32 rounding per certificate operation; the _rn intrinsics keep the
-// compiler from contracting or reassociating anything.
-template <int N>
-__device__ __forceinline__ VecF<N> vadd(const VecF<N>& a, const VecF<N>& b) {
+// One FP32 rounding per certificate operation, never contracted or
+// reassociated.  Pairs of lanes go through sm_100's packed FP32 instructions
+// (add/sub/mul.rn.f32x2: two independent IEEE single-precision operations,
+// round to nearest even, denormals kept -- the same results as two scalar
+// __fadd_rn / __fsub_rn / __fmul_rn), which halves the arithmetic issue of the
+// transforms and reconstructs; an odd last lane uses the scalar intrinsic.
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+template <int N, class Op2, class Op1>
+__device__ __forceinline__ VecF<N> vbinary(const VecF<N>& a, const VecF<N>& b, Op2 op2, Op1 op1) {
   VecF<N> r;
 #pragma unroll
-  for (int i = 0; i < N; ++i) r.v[i] = __fadd_rn(a.v[i], b.v[i]);
+  for (int i = 0; i + 1 < N; i += 2)
+    unpack_f32x2(op2(pack_f32x2(a.v[i], a.v[i + 1]), pack_f32x2(b.v[i], b.v[i + 1])), r.v[i], r.v[i + 1]);
+  if constexpr (N % 2 == 1) r.v[N - 1] = op1(a.v[N - 1], b.v[N - 1]);
   return r;
+}
+
+template <int N>
+__device__ __forceinline__ VecF<N> vadd(const VecF<N>& a, const VecF<N>& b) {
+  return vbinary<N>(a, b, [](uint64_t x, uint64_t y) { return add_f32x2(x, y); },
+                    [](float x, float y) { return __fadd_rn(x, y); });
 }
 template <int N>
 __device__ __forceinline__ VecF<N> vsub(const VecF<N>& a, const VecF<N>& b) {
-  VecF<N> r;
-#pragma unroll
-  for (int i = 0; i < N; ++i) r.v[i] = __fsub_rn(a.v[i], b.v[i]);
-  return r;
+  return vbinary<N>(a, b, [](uint64_t x, uint64_t y) { return sub_f32x2(x, y); },
+                    [](float x, float y) { return __fsub_rn(x, y); });
 }
 // Unary minus as 0 - x: a zero operand yields +0, matching the reference's
 // Triton kernels (they lower `-x` to a subtraction from zero).
 template <int N>
 __device__ __forceinline__ VecF<N> vneg(const VecF<N>& a) {
-  VecF<N> r;
+  VecF<N> zero;
 #pragma unroll
-  for (int i = 0; i < N; ++i) r.v[i] = __fsub_rn(0.0f, a.v[i]);
-  return r;
+  for (int i = 0; i < N; ++i) zero.v[i] = 0.0f;
+  return vsub(zero, a);
 }
 // Scaling by a power of two (or a small dyadic): exact, so x/2 == x*0.5.
 template <int N>
 __device__ __forceinline__ VecF<N> vscale(const VecF<N>& a, float c) {
-  VecF<N> r;
+  VecF<N> cv;
+#pragma unroll
+  for (int i = 0; i < N; ++i) cv.v[i] = c;
+  return vbinary<N>(a, cv, [](uint64_t x, uint64_t y) { return mul_f32x2(x, y); },
+                    [](float x, float y) { return __fmul_rn(x, y); });
+}
+
+// The same operations lane by lane in scalar FP32 instructions, for circuits
+// whose packed form needs more registers than a thread has: the rank-343
+// input sides (64 inputs and ~240 gates a position).
+template <int N>
+struct VecFs {
+  float v[N];
+};
+template <int N>
+__device__ __forceinline__ VecFs<N> vadd(const VecFs<N>& a, const VecFs<N>& b) {
+  VecFs<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = __fadd_rn(a.v[i], b.v[i]);
+  return r;
+}
+template <int N>
+__device__ __forceinline__ VecFs<N> vsub(const VecFs<N>& a, const VecFs<N>& b) {
+  VecFs<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = __fsub_rn(a.v[i], b.v[i]);
+  return r;
+}
+template <int N>
+__device__ __forceinline__ VecFs<N> vneg(const VecFs<N>& a) {
+  VecFs<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = __fsub_rn(0.0f, a.v[i]);
+  return r;
+}
+template <int N>
+__device__ __forceinline__ VecFs<N> vscale(const VecFs<N>& a, float c) {
+  VecFs<N> r;
 #pragma unroll
   for (int i = 0; i < N; ++i) r.v[i] = __fmul_rn(a.v[i], c);
   return r;
 }
+template <int N>
+__device__ __forceinline__ VecFs<N> to_scalar_math(const VecF<N>& a) {
+  VecFs<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = a.v[i];
+  return r;
+}
+template <int N>
+__device__ __forceinline__ VecF<N> to_packed_math(const VecFs<N>& a) {
+  VecF<N> r;
+#pragma unroll
+  for (int i = 0; i < N; ++i) r.v[i] = a.v[i];
+  return r;
+}
+// Programs with this many inputs run in scalar FP32 (see VecFs).
+constexpr int kScalarMathInputs = 64;
 
 template <int N>
 struct VecIO;
@@ -240,11 +327,19 @@ __device__ __forceinline__ void block_transform_body(const TransformArgs& a, uin
         }
       }
     }
-    auto in = [&](int q) -> VecF<VEC> { return unpack_in<kHalfIn, VEC>(raw[q]); };
-    auto out = [&](int o, const VecF<VEC>& x) {
-      store_plane_vec<kBfPlanes, VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
-    };
-    Prog::template run<VecF<VEC>>(in, out);
+    if constexpr (Prog::kInputs >= kScalarMathInputs) {
+      auto in = [&](int q) -> VecFs<VEC> { return to_scalar_math(unpack_in<kHalfIn, VEC>(raw[q])); };
+      auto out = [&](int o, const VecFs<VEC>& x) {
+        store_plane_vec<kBfPlanes, VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, to_packed_math(x));
+      };
+      Prog::template run<VecFs<VEC>>(in, out);
+    } else {
+      auto in = [&](int q) -> VecF<VEC> { return unpack_in<kHalfIn, VEC>(raw[q]); };
+      auto out = [&](int o, const VecF<VEC>& x) {
+        store_plane_vec<kBfPlanes, VEC>(dst + o * plane + static_cast<int64_t>(i) * ldd + j, x);
+      };
+      Prog::template run<VecF<VEC>>(in, out);
+    }
   }
 }
 
@@ -491,7 +586,7 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) right_transform_kn_kernel
     const int kk = (idx % kVecs) * VEC;
     const int64_t n = n0 + nn, k = k0 + kk;
     if (n >= bn || k >= ldk) continue;
-    auto in = [&](int q) -> VecF<VEC> {
+    auto load = [&](int q) -> VecF<VEC> {
       Raw raw;
       uint16_t* e = reinterpret_cast<uint16_t*>(&raw);
       const uint16_t* src = kn_tile + (q * TN + nn) * T::kPitch + kk;
@@ -499,10 +594,16 @@ __global__ void __launch_bounds__(THREADS, MIN_BLOCKS) right_transform_kn_kernel
       for (int v = 0; v < VEC; ++v) e[v] = src[v];
       return unpack_in<kHalfIn, VEC>(raw);
     };
-    auto out = [&](int o, const VecF<VEC>& x) {
+    auto store = [&](int o, const VecF<VEC>& x) {
       store_plane_vec<kBfPlanes, VEC>(dst + o * plane + n * ldk + k, x);
     };
-    Prog::template run<VecF<VEC>>(in, out);
+    if constexpr (Prog::kInputs >= kScalarMathInputs) {
+      auto in = [&](int q) -> VecFs<VEC> { return to_scalar_math(load(q)); };
+      auto out = [&](int o, const VecFs<VEC>& x) { store(o, to_packed_math(x)); };
+      Prog::template run<VecFs<VEC>>(in, out);
+    } else {
+      Prog::template run<VecF<VEC>>(load, store);
+    }
   }
 }
 
