@@ -182,9 +182,10 @@ def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch)
     assert torch.all((got - exact).abs() <= bound)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
 @pytest.mark.parametrize("variant", ["pair256", "pair256k128"])
 @pytest.mark.parametrize("rank,bm,bn,bk", [(3, 262, 300, 200), (2, 517, 260, 136), (48, 2054, 72, 64)])
-def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, monkeypatch):
+def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, dtype, monkeypatch):
     """A short last M band (bm % 256 <= 128) run as a second, 1-SM launch over
     the planes' last rows (FMM_LEAF_GEMM_TAIL=1 forces the split): the rows of
     the 2-SM band equal the single-launch products bit for bit, the band's rows
@@ -193,15 +194,15 @@ def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, monkeypatch
     monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
     g = torch.Generator().manual_seed(bm)
     ldk, ldp = -(-bk // 8) * 8, -(-bn // 8) * 8
-    L = torch.zeros((rank, bm, ldk), dtype=torch.float16)
-    Rt = torch.zeros((rank, bn, ldk), dtype=torch.float16)
-    L[:, :, :bk] = torch.randn((rank, bm, bk), generator=g).half()
-    Rt[:, :, :bk] = torch.randn((rank, bn, bk), generator=g).half()
+    L = torch.zeros((rank, bm, ldk), dtype=dtype)
+    Rt = torch.zeros((rank, bn, ldk), dtype=dtype)
+    L[:, :, :bk] = torch.randn((rank, bm, bk), generator=g).to(dtype)
+    Rt[:, :, :bk] = torch.randn((rank, bn, bk), generator=g).to(dtype)
     L, Rt = L.cuda(), Rt.cuda()
     outs = []
     for tail in ("0", "1"):
         monkeypatch.setenv("FMM_LEAF_GEMM_TAIL", tail)
-        P_all = torch.full((rank * bm * ldp + ldp,), float("nan"), device="cuda", dtype=torch.float16)
+        P_all = torch.full((rank * bm * ldp + ldp,), float("nan"), device="cuda", dtype=dtype)
         P = P_all[: rank * bm * ldp].view(rank, bm, ldp)
         _native.leaf_gemm(rank, L, Rt, bm, bn, bk, P)
         torch.cuda.synchronize()
@@ -212,7 +213,9 @@ def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, monkeypatch
     assert torch.equal(outs[0][:, :main].view(torch.int16), outs[1][:, :main].view(torch.int16))
     a, b = L[:, main:, :bk].double().cpu(), Rt[:, :, :bk].double().cpu().transpose(1, 2)
     exact = torch.matmul(a, b)
-    bound = torch.clamp(exact.abs(), min=2.0**-14) * 2.0**-10 + (bk + 2) * 2.0**-23 * torch.matmul(a.abs(), b.abs())
+    # one ulp of the product format (10 or 7 significand bits) + FP32 accumulation
+    ulp = 2.0**-10 if dtype == torch.float16 else 2.0**-7
+    bound = torch.clamp(exact.abs(), min=2.0**-14) * ulp + (bk + 2) * 2.0**-23 * torch.matmul(a.abs(), b.abs())
     assert torch.all((outs[1][:, main:].cpu().double() - exact).abs() <= bound)
 
 
