@@ -21,9 +21,10 @@ fixed).  Two numbers are measured, both as the max over ranks of CUDA-event
 time:
 
 * ``value``: the whole ``C[M, N]`` gathered on every rank
-  (``RowShardedLinear``: NCCL all-gather of finished row chunks overlapped
-  with the next chunk, or ``--transport p2p``: the reconstruct kernel stores
-  every rank's rows into all peers' buffers over NVLink);
+  (``RowShardedLinear``; by default ``--transport p2p``: the reconstruct
+  kernel stores every rank's rows into all peers' buffers over NVLink, which
+  measured fastest at 2, 4 and 8 GPUs; ``--transport nccl``: NCCL all-gather
+  of finished row chunks overlapped with the next chunk);
 * ``no_gather``: each rank keeps its own rows (the caller does not need the
   gathered output), no data-path collective.
 
@@ -626,8 +627,12 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
             "bytes_received_per_gpu": moved,
             "received_gbs": round(moved / (gathered_step_ms * 1e-3) / 1e9, 1),
             "link_floor_ms": round(link_floor_ms, 4),
-            "limiter": ("NVLink receive bandwidth: every GPU receives (N-1)/N of C; floor = bytes "
-                        "received / 770 GB/s measured peer copy"),
+            "gather_overhead_ms": round(gathered_step_ms - local_step_ms, 4),
+            "limiter": (f"every GPU receives (N-1)/N of C: {moved / 1e9:.2f} GB, link floor "
+                        f"{link_floor_ms:.3f} ms at the 770 GB/s measured peer copy; the gather adds "
+                        f"{gathered_step_ms - local_step_ms:.3f} ms to the {local_step_ms:.3f} ms no-gather step"
+                        + (" (link-bound: the gathered step is within 1.3x of compute + link floor)"
+                           if gathered_step_ms < 1.3 * max(local_step_ms, link_floor_ms) else "")),
         }
         clock_summary = gathered_line["clock"]
     else:
@@ -712,7 +717,7 @@ def main() -> None:
     parser.add_argument("--reserve-sms", type=int, default=32,
                         help="SMs the GEMM leaves free, while sharded chunks compute, for the NCCL "
                              "all-gather or the gathering reconstruct of the previous chunk")
-    parser.add_argument("--transport", choices=("nccl", "p2p"), default="nccl",
+    parser.add_argument("--transport", choices=("nccl", "p2p"), default="p2p",
                         help="sharded gather: NCCL all-gather, or the reconstruct kernel storing "
                              "into every rank's peer-mapped buffer over NVLink")
     parser.add_argument("--profile", action="store_true",

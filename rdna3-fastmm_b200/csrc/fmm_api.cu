@@ -819,25 +819,19 @@ int launch_leaf_band(int variant, bool tma_store, int rank, const uint16_t* L, c
   return launch_single<kBf16>(band_l, Rt, prm, ldk, sms, stream);
 }
 
-// Rows of a short last M tile of the 2-SM GEMM: when the planes' last 256-row
-// tile holds at most 128 rows (c4: bm = 2054, 6 rows), those rows go to a
-// second, 1-SM launch of 128-row tiles, which spends one SM instead of two
-// on each of them; used when the cost model counts fewer tile waves for the
-// two launches together.  FMM_LEAF_GEMM_TAIL=0 keeps one launch, =1 splits
-// whenever the last tile qualifies.
-int64_t split_tail_rows(int variant, int64_t rank, int64_t bm, int64_t bn, int sms) {
+// Rows of a short last M tile of the 2-SM GEMM, run as a second, 1-SM launch
+// of 128-row tiles over the planes' last rows (one SM instead of two for each
+// of their tiles) when FMM_LEAF_GEMM_TAIL=1 and the planes' last 256-row tile
+// holds at most 128 rows.  Off by default: on c4 (bm = 2054, a 6-row last
+// tile) the two launches measured 0.7 % slower than one (0.591 vs 0.587 ms,
+// GEMM alone, three interleaved rounds) -- the second launch's partial waves
+// cost what the narrower tiles save.
+int64_t split_tail_rows(int variant, int64_t bm) {
   if (variant == kVariantSingle) return 0;
   const int64_t tail = bm % 256;
   if (bm < 256 || tail == 0 || tail > 128) return 0;
-  if (const char* v = std::getenv("FMM_LEAF_GEMM_TAIL")) {
-    if (std::string(v) == "0") return 0;
-    if (std::string(v) == "1") return tail;
-  }
-  const int cost_variant = variant == kVariantPair256K128 ? int(kVariantPair256) : variant;
-  const double whole = variant_cost(cost_variant, rank, bm, bn, sms);
-  const double split = variant_cost(cost_variant, rank, bm - tail, bn, sms) +
-                       variant_cost(kVariantSingle, rank, tail, bn, sms);
-  return split < whole ? tail : 0;
+  const char* v = std::getenv("FMM_LEAF_GEMM_TAIL");
+  return (v != nullptr && std::string(v) == "1") ? tail : 0;
 }
 
 // FP16 planes (kBf16 = false) or BF16 planes.  The BF16 form carries the
@@ -864,7 +858,7 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   if (variant == kVariantPair256 && bk >= 3072) variant = kVariantPair256K128;
   const uint16_t* l16 = static_cast<const uint16_t*>(L);
   uint16_t* p16 = static_cast<uint16_t*>(P);
-  const int64_t tail = split_tail_rows(variant, rank, bm, bn, sms);
+  const int64_t tail = split_tail_rows(variant, bm);
   if (int rc = launch_leaf_band<kBf16>(variant, tma_store, rank, l16, Rt, 0, bm - tail, bm, bn, bk, p16, sms,
                                        stream))
     return rc;
