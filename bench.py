@@ -600,9 +600,8 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         "dtype": "bf16 in/out, fp16 leaves, fp32 accumulate",
         "data": "synthetic (seeded A~N(0,1), W~N(0,0.02) BF16)",
     }
-    config = {"workload": f"{args.workload}: {description}", "scheme": scheme,
-              "M": M_total, "K": K, "N": N, "bias": with_bias, "prepacked": prepacked,
-              "l2": "flushed (256 MiB write) before every step"}
+    config = dict(workload_config(args))
+    config["l2"] = "flushed (256 MiB write) before every step"
     if shard:
         gathered_step_ms = g_total / args.steps
         moved = (world - 1) * M * N * 2  # bytes each rank receives
@@ -668,6 +667,16 @@ def _emit(line: dict) -> None:
 _JSON_FD = 1
 
 
+def workload_config(args) -> dict:
+    """The workload keys both arms report (the same dict for the same flags)."""
+    scheme, M, K, N, with_bias, prepacked, description = WORKLOADS[args.workload]
+    if args.rows:
+        M = args.rows
+        description += f" (rows overridden to {M})"
+    return {"workload": f"{args.workload}: {description}", "scheme": scheme, "M": M, "K": K, "N": N,
+            "bias": with_bias, "prepacked": prepacked}
+
+
 def reference_arm(args) -> None:
     """The reference's algorithm on the host cores (CPU oracle, all threads):
     each step one bounded sample; at most 5 so the arm ends within minutes."""
@@ -679,9 +688,11 @@ def reference_arm(args) -> None:
         "impl": "reference",
         "metric": METRIC,
         "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 and not args.replicas else "weak", "vs_baseline": None,
         "dtype": "bf16 in/out, fp16 leaves", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {WORKLOADS[args.workload][6]}"},
+        "config": {**workload_config(args),
+                   "parallelism": "the reference's algorithm on the host cores (rank 0 alone)"},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
