@@ -571,19 +571,16 @@ int choose_variant(int64_t rank, int64_t bm, int64_t bn, int sms) {
 }
 
 // Epilogue of the 256 x 256 pair GEMM: per-lane row stores, or shared-memory
-// staged TMA stores (16 KiB of buffers, which costs the 64-deep configuration
-// one of its 7 stages).  Measured on B200 (GEMM alone, full clock, L2 flushed):
-// the TMA stores win where the epilogue of one tile is long against the main
-// loop of the next -- short leaves (c5b, bk = 1152: +8 %) -- and wherever the
-// stage count does not change (128-deep k-blocks, bk >= 3072: c4 +2.5 %, c3
-// +1 %); at bk = 2048 the seventh stage is worth more (c2 -3 %, c5a +-3 %).
-// FMM_LEAF_GEMM_EPILOGUE=rows|tma forces one.
-bool tma_store_epilogue(int64_t bk) {
+// staged TMA stores (16 KiB of buffers).  The 128-deep configuration keeps its
+// 3 stages either way and takes the TMA stores; the 64-deep one would lose one
+// of its 7 stages and keeps the row stores.  FMM_LEAF_GEMM_EPILOGUE=rows|tma
+// forces either.
+bool tma_store_epilogue(int variant) {
   if (const char* v = std::getenv("FMM_LEAF_GEMM_EPILOGUE")) {
     if (std::string(v) == "tma") return true;
     if (std::string(v) == "rows") return false;
   }
-  return bk >= 3072 || bk < 2048;
+  return variant == kVariantPair256K128;
 }
 
 template <class Kernel>
@@ -852,10 +849,14 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   const int sms = usable_sms(info);
   int variant = choose_variant(rank, bm, bn, sms);
   if (kBf16 && (variant == kVariantPair192 || variant == kVariantPair128)) variant = kVariantPair256;
-  const bool tma_store = tma_store_epilogue(bk);
-  // deep leaves: 128-deep k-blocks in 3 stages (half the barrier round trips per
-  // FLOP) measured 0.3-2.8 % faster from bk = 3072 up and 1-3 % slower below
-  if (variant == kVariantPair256 && bk >= 3072) variant = kVariantPair256K128;
+  // 128-deep k-blocks in 3 stages with the TMA-store epilogue, from bk = 1024
+  // up (at most 6 % of the last k-block's MMA work is zero padding there):
+  // measured against 64-deep k-blocks in 7 stages with row stores (GEMM alone,
+  // full clock, L2 flushed, 3 interleaved rounds): c2 0.256 -> 0.240 ms, c5a
+  // 0.594 -> 0.557, c5b 4.11-4.17 -> 3.95-4.09 (against 64-deep k-blocks with
+  // the TMA stores there, the previous choice)
+  if (variant == kVariantPair256 && bk >= 1024) variant = kVariantPair256K128;
+  const bool tma_store = tma_store_epilogue(variant);
   const uint16_t* l16 = static_cast<const uint16_t*>(L);
   uint16_t* p16 = static_cast<uint16_t*>(P);
   const int64_t tail = split_tail_rows(variant, bm);
