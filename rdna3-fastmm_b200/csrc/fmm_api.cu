@@ -781,6 +781,17 @@ int launch_single(const void* L, const void* Rt, const LeafGemmParams& prm, int6
   return FMM_OK;
 }
 
+// M-tiles per group of the tile order (a group sweeps all N-tiles of its
+// M-tiles before the next group starts, so the group's L rows and the
+// weight planes' N-tiles are reused from L2): 16, or FMM_LEAF_GEMM_GROUP_M.
+int leaf_group_m() {
+  if (const char* v = std::getenv("FMM_LEAF_GEMM_GROUP_M")) {
+    const int g = std::atoi(v);
+    if (g >= 1 && g <= 4096) return g;
+  }
+  return 16;
+}
+
 // One GEMM launch over rows [row0, row0 + rows) of every plane (planes of
 // `plane_rows` rows), with the given variant and epilogue.
 template <bool kBf16>
@@ -798,7 +809,7 @@ int launch_leaf_band(int variant, bool tma_store, int rank, const uint16_t* L, c
   prm.rank = rank;
   prm.tiles_m = static_cast<int32_t>(ceil_div(rows, kGemmBM));
   prm.tiles_n = static_cast<int32_t>(ceil_div(bn, GemmCfg::kBN));
-  prm.group_m = 16;
+  prm.group_m = leaf_group_m();
   prm.P = P + row0 * ldp;
   prm.timeout_ns = g_timeout_ns;
   if (variant == kVariantPair256) {
@@ -855,7 +866,9 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   // full clock, L2 flushed, 3 interleaved rounds): c2 0.256 -> 0.240 ms, c5a
   // 0.594 -> 0.557, c5b 4.11-4.17 -> 3.95-4.09 (against 64-deep k-blocks with
   // the TMA stores there, the previous choice)
-  if (variant == kVariantPair256 && bk >= 1024) variant = kVariantPair256K128;
+  // (a forced FMM_LEAF_GEMM_VARIANT=pair256 keeps 64-deep k-blocks)
+  if (variant == kVariantPair256 && bk >= 1024 && std::getenv("FMM_LEAF_GEMM_VARIANT") == nullptr)
+    variant = kVariantPair256K128;
   const bool tma_store = tma_store_epilogue(variant);
   const uint16_t* l16 = static_cast<const uint16_t*>(L);
   uint16_t* p16 = static_cast<uint16_t*>(P);
