@@ -792,6 +792,12 @@ int leaf_group_m() {
   return 16;
 }
 
+// Serpentine N order across tile groups (FMM_LEAF_GEMM_SERPENTINE=1).
+int leaf_serpentine() {
+  const char* v = std::getenv("FMM_LEAF_GEMM_SERPENTINE");
+  return (v != nullptr && std::string(v) == "1") ? 1 : 0;
+}
+
 // One GEMM launch over rows [row0, row0 + rows) of every plane (planes of
 // `plane_rows` rows), with the given variant and epilogue.
 template <bool kBf16>
@@ -810,6 +816,7 @@ int launch_leaf_band(int variant, bool tma_store, int rank, const uint16_t* L, c
   prm.tiles_m = static_cast<int32_t>(ceil_div(rows, kGemmBM));
   prm.tiles_n = static_cast<int32_t>(ceil_div(bn, GemmCfg::kBN));
   prm.group_m = leaf_group_m();
+  prm.serpentine = leaf_serpentine();
   prm.P = P + row0 * ldp;
   prm.timeout_ns = g_timeout_ns;
   if (variant == kVariantPair256) {

@@ -50,13 +50,15 @@ struct LeafGemmParams {
   int32_t rank;
   int32_t tiles_m, tiles_n;
   int32_t group_m;
+  int32_t serpentine;  // odd groups sweep the N-tiles in reverse
   uint16_t* P;  // FP16 (or BF16) products
   uint64_t timeout_ns;
 };
 
 // Tile t -> (r, tm, tn): batches in order, inside a batch groups of
 // `group_m` M-tiles sweep the N-tiles so concurrently running CTAs share L
-// rows and Rt columns in L2.
+// rows and Rt columns in L2; with `serpentine` every odd group sweeps them in
+// reverse, so a group starts on the Rt columns its predecessor used last.
 __device__ __forceinline__ void leaf_tile_coords(const LeafGemmParams& p, int t, int& r, int& tm,
                                                  int& tn) {
   const int per_batch = p.tiles_m * p.tiles_n;
@@ -69,6 +71,7 @@ __device__ __forceinline__ void leaf_tile_coords(const LeafGemmParams& p, int t,
   const int in_group = local - group * per_group;
   tm = first_m + in_group % group_rows;
   tn = in_group / group_rows;
+  if (p.serpentine && (group & 1)) tn = p.tiles_n - 1 - tn;
 }
 
 // Columns the MMA computes for N tile tn: the whole tile, or for the ragged

@@ -182,6 +182,31 @@ def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch)
     assert torch.all((got - exact).abs() <= bound)
 
 
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair256k128"])
+def test_leaf_gemm_tile_order_does_not_change_products(variant, monkeypatch):
+    """Group sizes and the serpentine N order only reorder whole tiles: the
+    products are bitwise those of the default order."""
+    monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
+    rank, bm, bn, bk = 3, 700, 900, 520
+    g = torch.Generator().manual_seed(7)
+    ldk, ldp = -(-bk // 8) * 8, -(-bn // 8) * 8
+    L = torch.zeros((rank, bm, ldk), dtype=torch.float16)
+    Rt = torch.zeros((rank, bn, ldk), dtype=torch.float16)
+    L[:, :, :bk] = torch.randn((rank, bm, bk), generator=g).half()
+    Rt[:, :, :bk] = torch.randn((rank, bn, bk), generator=g).half()
+    L, Rt = L.cuda(), Rt.cuda()
+    outs = []
+    for group_m, serpentine in (("16", "0"), ("1", "1"), ("2", "1"), ("2", "0")):
+        monkeypatch.setenv("FMM_LEAF_GEMM_GROUP_M", group_m)
+        monkeypatch.setenv("FMM_LEAF_GEMM_SERPENTINE", serpentine)
+        P = torch.full((rank, bm, ldp), float("nan"), device="cuda", dtype=torch.float16)
+        _native.leaf_gemm(rank, L, Rt, bm, bn, bk, P)
+        torch.cuda.synchronize()
+        outs.append(P[:, :, :bn].clone())
+    for other in outs[1:]:
+        assert torch.equal(outs[0].view(torch.int16), other.view(torch.int16))
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
 @pytest.mark.parametrize("variant", ["pair256", "pair256k128"])
 @pytest.mark.parametrize("rank,bm,bn,bk", [(3, 262, 300, 200), (2, 517, 260, 136), (48, 2054, 72, 64)])
