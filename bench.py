@@ -487,7 +487,7 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
     if shard:
         from rdna3_fastmm.distributed import RowShardedLinear
 
-        p2p = args.transport == "p2p"
+        p2p = args.transport in ("p2p", "ce")  # the layer gathers into its own peer-mapped buffer
         layer = RowShardedLinear(plan_type, M_total, W, bias=bias, chunks=args.chunks,
                                  reserve_sms=args.reserve_sms, max_free_memory_fraction=0.9,
                                  transport=args.transport)
@@ -613,8 +613,10 @@ def run_native(args, rank: int, world: int, device) -> dict | None:
         })
         config.update({"rows_per_gpu": M, "chunks": args.chunks,
                        "parallelism": f"rows sharded x{world}, packed weight replicated, output gathered "
-                                      + ("by the reconstruct over NVLink peer memory" if args.transport == "p2p"
-                                         else "by NCCL all-gather overlapped with the next chunk")})
+                                      + {"p2p": "by the reconstruct storing into NVLink peer memory",
+                                         "ce": "by copy-engine copies into NVLink peer memory, overlapped "
+                                               "with the next chunk",
+                                         "nccl": "by NCCL all-gather overlapped with the next chunk"}[args.transport]})
         line["no_gather"] = {
             "value": round(job_flops / (local_step_ms * 1e-3) / 1e12, 2),
             "ms_per_step": round(local_step_ms, 4),
@@ -730,9 +732,10 @@ def main() -> None:
     parser.add_argument("--reserve-sms", type=int, default=32,
                         help="SMs the GEMM leaves free, while sharded chunks compute, for the NCCL "
                              "all-gather or the gathering reconstruct of the previous chunk")
-    parser.add_argument("--transport", choices=("nccl", "p2p"), default="p2p",
-                        help="sharded gather: NCCL all-gather, or the reconstruct kernel storing "
-                             "into every rank's peer-mapped buffer over NVLink")
+    parser.add_argument("--transport", choices=("nccl", "p2p", "ce"), default="p2p",
+                        help="sharded gather: NCCL all-gather, the reconstruct kernel storing "
+                             "into every rank's peer-mapped buffer over NVLink (p2p), or copy-engine "
+                             "copies into the peers' buffers behind each chunk (ce)")
     parser.add_argument("--profile", action="store_true",
                         help="timed steps only: no cuBLAS, e2e or CPU legs")
     args = parser.parse_args()

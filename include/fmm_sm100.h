@@ -174,6 +174,13 @@ int fmm_ipc_export(const void* ptr, unsigned char* handle, uint64_t* offset);
 int fmm_ipc_import(const unsigned char* handle, uint64_t offset, void** base, void** ptr);
 int fmm_ipc_close(void* base);
 
+/* Queue one device-to-device copy of `bytes` on `stream`; `dst` may be a
+ * peer's buffer mapped by fmm_ipc_import, so the copy engines carry it over
+ * NVLink while the SMs compute (the copy-engine gather of a row-sharded
+ * linear).  One cudaMemcpyAsync; nothing is allocated.  No reference
+ * counterpart (the reference is single-GPU). */
+int fmm_copy_async(void* dst, const void* src, uint64_t bytes, fmm_stream_t stream);
+
 /* The whole product through the scheme, using the caller's planes (L, Rt, P
  * sized by fmm_plan_dims): C = A * weight^T (+ bias) for F.linear, or, with
  * FMM_RIGHT_KN, C = A * B for a contiguous B[K,N].  With FMM_LINEAR_PREPACKED,

@@ -1139,6 +1139,15 @@ int fmm_ipc_close(void* base) {
   return FMM_OK;
 }
 
+int fmm_copy_async(void* dst, const void* src, uint64_t bytes, fmm_stream_t stream) {
+  if (dst == nullptr || src == nullptr) return fail(FMM_ERR_INVALID_ARGUMENT, "null pointer");
+  if (bytes == 0) return FMM_OK;
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (device to device)");
+  return FMM_OK;
+}
+
 int fmm_set_sm_budget(int sms) {
   if (sms < 0) return fail(FMM_ERR_INVALID_ARGUMENT, "SM budget must be >= 0");
   g_sm_budget = sms;

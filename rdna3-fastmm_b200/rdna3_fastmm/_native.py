@@ -67,6 +67,7 @@ _SIGNATURES = {
         ctypes.c_int,
     ),
     "fmm_ipc_close": ([_P], ctypes.c_int),
+    "fmm_copy_async": ([_P, _P, ctypes.c_uint64, _P], ctypes.c_int),
     "fmm_transform_aw": (
         [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P], ctypes.c_int,
     ),
@@ -220,6 +221,11 @@ def ipc_import(handle: bytes, offset: int) -> tuple[int, int]:
 
 def ipc_close(base: int) -> None:
     check(library().fmm_ipc_close(base), "fmm_ipc_close")
+
+
+def copy_async(dst: int, src: int, nbytes: int, stream: int) -> None:
+    """Device-to-device copy (``dst`` may be a peer mapping) queued on ``stream``."""
+    check(library().fmm_copy_async(dst, src, nbytes, stream), "fmm_copy_async")
 
 
 def reconstruct_gather(scheme: str, P, M: int, N: int, bias, dests: list[int], ldc: int, dtype) -> None:

@@ -26,6 +26,13 @@ tensor-core work without reserving SMs for a collective.  A one-element
 all-reduce queued behind the kernels makes every peer's rows visible before
 the result is used.
 
+``transport="ce"`` keeps the reconstruct local (each chunk's rows land in this
+rank's own IPC-exported output buffer) and hands the transfer to the copy
+engines: one device-to-device copy per peer and chunk (``fmm_copy_async``) on
+a stream of its own, into the peer's mapped buffer.  The copies of chunk c run
+while chunk c + 1 transforms, multiplies and reconstructs, and no SM is spent
+on the transfer; the same all-reduce ends the call.
+
 The reference is single-GPU; this is the path's multi-GPU form (M sharded
 across 1/2/4/8 GPUs, weight replicated, output gathered on demand).
 """
@@ -68,10 +75,10 @@ class RowShardedLinear:
                  bias: Optional[torch.Tensor] = None, chunks: int = 1, reserve_sms: int = 0,
                  local_linear: Optional[Callable[[torch.Tensor, torch.Tensor], None]] = None,
                  max_free_memory_fraction: float = 0.75, transport: str = "nccl") -> None:
-        if transport not in ("nccl", "p2p"):
-            raise ValueError("transport must be 'nccl' or 'p2p'")
-        if transport == "p2p" and local_linear is not None:
-            raise ValueError("the p2p transport runs the B200 plan, not a local stand-in")
+        if transport not in ("nccl", "p2p", "ce"):
+            raise ValueError("transport must be 'nccl', 'p2p' or 'ce'")
+        if transport in ("p2p", "ce") and local_linear is not None:
+            raise ValueError("the p2p and ce transports run the B200 plan, not a local stand-in")
         self.transport = transport
         self.group = group
         self.world = dist.get_world_size(group)
@@ -105,7 +112,7 @@ class RowShardedLinear:
             self.packed = self.plan.pack_weight(weight, max_free_memory_fraction)
             self.workspace = self.plan.allocate_workspace(max_free_memory_fraction, prepacked_right=True)
             self._local = self._plan_linear
-        if transport == "p2p":
+        if transport in ("p2p", "ce"):
             self._setup_p2p(max_free_memory_fraction)
 
     def _setup_p2p(self, max_free_memory_fraction: float) -> None:
@@ -132,15 +139,19 @@ class RowShardedLinear:
         # a second product workspace so chunk c's gathering reconstruct can
         # read its products while chunk c + 1 multiplies
         self._products = [self.workspace.products]
-        if self.chunks > 1:
+        if self.chunks > 1 and self.transport == "p2p":
             self._products.append(torch.empty_like(self.workspace.products))
         self._side = torch.cuda.Stream(device=self.device)
+        # ce: one copy stream per peer, so the copies to different peers run on
+        # separate copy engines at once
+        self._copy_streams = ([torch.cuda.Stream(device=self.device) for _ in range(self.world - 1)]
+                              if self.transport == "ce" else [])
         self._flag = torch.zeros(1, device=self.device, dtype=torch.int32)
 
     def close(self) -> None:
         """Unmap the peers' buffers (p2p transport).  Collective: no rank frees
         its gather buffer while a peer could still write into it."""
-        if self.transport != "p2p" or not self._ipc_bases:
+        if self.transport not in ("p2p", "ce") or not self._ipc_bases:
             return
         from . import _native
 
@@ -193,6 +204,28 @@ class RowShardedLinear:
             done[k] = torch.cuda.Event()
             done[k].record(self._side)
 
+    def _ce(self, local_rows: torch.Tensor) -> torch.Tensor:
+        from . import _native
+
+        main = torch.cuda.current_stream(self.device)
+        row_bytes = self.columns * 2
+        own = self._gather_out
+        peers = [base for peer, base in enumerate(self._peer_bases) if peer != self.rank]
+        ch = self.chunk_rows
+        for c, (start, count) in enumerate(self.row_blocks()):
+            self._plan_linear(local_rows[c * ch:c * ch + count], own[start:start + count])
+            ready = torch.cuda.Event()
+            ready.record(main)
+            src = own.data_ptr() + start * row_bytes
+            for stream, base in zip(self._copy_streams, peers):
+                stream.wait_event(ready)
+                _native.copy_async(base + start * row_bytes, src, count * row_bytes, stream.cuda_stream)
+        for stream in self._copy_streams:
+            main.wait_stream(stream)
+        # completion: as for p2p, an all-reduce queued behind this rank's copies
+        dist.all_reduce(self._flag, group=self.group)
+        return own
+
     def _plan_linear(self, local_rows: torch.Tensor, out: torch.Tensor) -> None:
         self.plan.run_linear_packed(local_rows, self.packed, self.workspace, self.bias, out)
 
@@ -237,10 +270,10 @@ class RowShardedLinear:
             raise ValueError(f"local rows have shape {tuple(local_rows.shape)}, "
                              f"expected {(self.count, self.inner)}")
         ch = self.chunk_rows
-        if gather and self.transport == "p2p":
+        if gather and self.transport in ("p2p", "ce"):
             if out is not None:
-                raise ValueError("the p2p transport gathers into its own peer-mapped buffer")
-            return self._p2p(local_rows)
+                raise ValueError("the p2p and ce transports gather into their own peer-mapped buffer")
+            return self._p2p(local_rows) if self.transport == "p2p" else self._ce(local_rows)
         if not gather:
             result = out if out is not None else torch.empty(
                 (self.count, self.columns), device=self.device, dtype=torch.bfloat16)

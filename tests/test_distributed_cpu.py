@@ -104,8 +104,9 @@ def test_transport_arguments_are_validated():
 
         with pytest.raises(ValueError, match="transport"):
             RowShardedLinear(None, 16, W, local_linear=local, transport="nvshmem")
-        with pytest.raises(ValueError, match="p2p transport runs the B200 plan"):
-            RowShardedLinear(None, 16, W, local_linear=local, transport="p2p")
+        for transport in ("p2p", "ce"):
+            with pytest.raises(ValueError, match="transports run the B200 plan"):
+                RowShardedLinear(None, 16, W, local_linear=local, transport=transport)
         layer = RowShardedLinear(None, 16, W, local_linear=local, transport="nccl")
         assert layer.transport == "nccl"
     finally:

@@ -1,7 +1,8 @@
 """Row-sharded linear on 2 B200s (skipped with fewer GPUs): the fused
 reconstruct + all-gather over NVLink peer memory (``transport="p2p"``, CUDA
-IPC mappings) must give bit for bit the rows of the reconstruct + NCCL
-all-gather path, on every rank, with and without chunking and bias."""
+IPC mappings) and the copy-engine gather (``transport="ce"``) must give bit for
+bit the rows of the reconstruct + NCCL all-gather path, on every rank, with and
+without chunking and bias."""
 
 import datetime
 import os
@@ -34,7 +35,7 @@ def _worker(rank: int, world: int, port: int, case: tuple, results) -> None:
     device = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=device)
-    p2p = None
+    p2p = ce = None
     try:
         scheme, M, K, N, chunks, with_bias = case
         plan_type = {"rank7": Rank7Plan, "rank48": Rank48Plan}[scheme]
@@ -43,10 +44,13 @@ def _worker(rank: int, world: int, port: int, case: tuple, results) -> None:
         bias = bias.to(device) if bias is not None else None
         nccl = RowShardedLinear(plan_type, M, W, bias=bias, chunks=chunks)
         p2p = RowShardedLinear(plan_type, M, W, bias=bias, chunks=chunks, transport="p2p")
+        ce = RowShardedLinear(plan_type, M, W, bias=bias, chunks=chunks, transport="ce")
         rows = nccl.local_rows(A)
         expected = nccl(rows)[:M].clone()
         got = p2p(rows).clone()
         got2 = p2p(rows).clone()  # the second call reuses the mapped buffers
+        got_ce = ce(rows).clone()
+        got_ce2 = ce(rows).clone()
         torch.cuda.synchronize()
         ref = torch.nn.functional.linear(A.float(), W.float(), None if bias is None else bias.float())
         err = float(torch.linalg.vector_norm(got.float() - ref) / torch.linalg.vector_norm(ref))
@@ -54,11 +58,14 @@ def _worker(rank: int, world: int, port: int, case: tuple, results) -> None:
             "shape": tuple(got.shape) == (M, N),
             "equal": bool(torch.equal(got.view(torch.int16), expected.view(torch.int16))),
             "equal_again": bool(torch.equal(got2.view(torch.int16), expected.view(torch.int16))),
+            "ce_equal": bool(torch.equal(got_ce.view(torch.int16), expected.view(torch.int16))
+                             and torch.equal(got_ce2.view(torch.int16), expected.view(torch.int16))),
             "err": err,
         }
     finally:
-        if p2p is not None:
-            p2p.close()
+        for layer in (p2p, ce):
+            if layer is not None:
+                layer.close()
         dist.destroy_process_group()
 
 
@@ -75,5 +82,5 @@ def test_p2p_gather_matches_nccl_gather(case):
         results = dict(results)
     for rank in range(2):
         r = results[rank]
-        assert r["shape"] and r["equal"] and r["equal_again"], (rank, case, r)
+        assert r["shape"] and r["equal"] and r["equal_again"] and r["ce_equal"], (rank, case, r)
         assert r["err"] < 5e-3, (rank, case, r)
