@@ -311,10 +311,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //   warp 1   TMEM allocation for the pair (both CTAs); in the even CTA one
 //            thread issues the MMAs and the multicast commits.
 //   warps 2-5 epilogue: each CTA drains its own 128 accumulator lanes and
-//            signals the even CTA's `tmem_empty` barrier (8 arrivals).
-// No TMA multicast is used: every CTA loads only its own halves.  Deep leaves
-// (bk >= 3072) use 128-deep k-blocks in 3 stages: two 64-deep atom columns per
-// operand and stage, half the barrier round trips per FLOP.
+//            signals the even CTA's `tmem_empty` barrier (8 arrivals); the
+//            products leave as 16-byte row stores, or (TMA_STORE) as 32 x 32
+//            blocks staged in shared memory and written by TMA stores.
+// No TMA multicast is used: every CTA loads only its own halves.  Leaves with
+// bk >= 1024 run 128-deep k-blocks in 3 stages (two 64-deep atom columns per
+// operand and stage, half the barrier round trips per FLOP) with the TMA-store
+// epilogue; the host picks the configuration (fmm_api.cu).
 template <int BN, int STAGES, int BK = kGemmBK, bool TMA_STORE = false>
 struct LeafGemmPairConfig {
   static constexpr int kBN = BN;
