@@ -1,7 +1,7 @@
 """Benchmark of the reduced-rank BF16 linear on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c4r49|c5a|c5b]
-                    [--impl native|reference] [--replicas] [--transport nccl|p2p]
+                    [--impl native|reference] [--replicas] [--transport nccl|p2p|ce]
 
 Default workload: c5b, ``A[65536,4608] x W[12288,4608]^T`` through the rank-48
 prepacked plan -- the largest configuration of the benchmark set that fits one
@@ -21,10 +21,12 @@ fixed).  Two numbers are measured, both as the max over ranks of CUDA-event
 time:
 
 * ``value``: the whole ``C[M, N]`` gathered on every rank
-  (``RowShardedLinear``; by default ``--transport p2p``: the reconstruct
-  kernel stores every rank's rows into all peers' buffers over NVLink, which
-  measured fastest at 2, 4 and 8 GPUs; ``--transport nccl``: NCCL all-gather
-  of finished row chunks overlapped with the next chunk);
+  (``RowShardedLinear``; by default the transport measured fastest at that
+  GPU count: at 2 GPUs ``ce`` -- each finished row chunk copied into the peer's
+  buffer by the copy engines while the next chunk computes -- and from 3 GPUs
+  up ``p2p`` -- the reconstruct kernel stores every rank's rows into all
+  peers' buffers over NVLink; ``--transport nccl``: NCCL all-gather of
+  finished row chunks overlapped with the next chunk);
 * ``no_gather``: each rank keeps its own rows (the caller does not need the
   gathered output), no data-path collective.
 
@@ -732,14 +734,19 @@ def main() -> None:
     parser.add_argument("--reserve-sms", type=int, default=32,
                         help="SMs the GEMM leaves free, while sharded chunks compute, for the NCCL "
                              "all-gather or the gathering reconstruct of the previous chunk")
-    parser.add_argument("--transport", choices=("nccl", "p2p", "ce"), default="p2p",
+    parser.add_argument("--transport", choices=("nccl", "p2p", "ce"), default=None,
                         help="sharded gather: NCCL all-gather, the reconstruct kernel storing "
                              "into every rank's peer-mapped buffer over NVLink (p2p), or copy-engine "
-                             "copies into the peers' buffers behind each chunk (ce)")
+                             "copies into the peers' buffers behind each chunk (ce); default: the "
+                             "fastest measured at that GPU count (ce at 2 GPUs, p2p from 3 up)")
     parser.add_argument("--profile", action="store_true",
                         help="timed steps only: no cuBLAS, e2e or CPU legs")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.transport is None:
+        # c5b at 2 GPUs: ce 3.21 ms, p2p 3.40; at 8: p2p 2.75 ms, ce 3.83-4.85
+        # (the copy engines do not keep up with seven peers at once)
+        args.transport = "ce" if int(os.environ.get("WORLD_SIZE", "1")) == 2 else "p2p"
     if args.chunks is None:
         args.chunks = 1 if args.transport == "p2p" else 4
 
