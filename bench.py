@@ -671,6 +671,14 @@ def _emit(line: dict) -> None:
 _JSON_FD = 1
 
 
+def default_transport(world: int) -> str:
+    """Gather transport measured fastest at this GPU count (c5b): at 2 GPUs the
+    copy engines (ce 3.21 ms, p2p 3.40), from 3 up the fused reconstruct (at 8:
+    p2p 2.75 ms, ce 3.83-4.85 -- the copy engines do not keep up with seven
+    peers at once)."""
+    return "ce" if world == 2 else "p2p"
+
+
 def workload_config(args) -> dict:
     """The workload keys both arms report (the same dict for the same flags)."""
     scheme, M, K, N, with_bias, prepacked, description = WORKLOADS[args.workload]
@@ -744,9 +752,7 @@ def main() -> None:
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.transport is None:
-        # c5b at 2 GPUs: ce 3.21 ms, p2p 3.40; at 8: p2p 2.75 ms, ce 3.83-4.85
-        # (the copy engines do not keep up with seven peers at once)
-        args.transport = "ce" if int(os.environ.get("WORLD_SIZE", "1")) == 2 else "p2p"
+        args.transport = default_transport(int(os.environ.get("WORLD_SIZE", "1")))
     if args.chunks is None:
         args.chunks = 1 if args.transport == "p2p" else 4
 
