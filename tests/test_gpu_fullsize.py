@@ -11,10 +11,12 @@ of the path is position-wise, so sampled positions pin the full-size launch:
 * row ``i`` of the products and the output rows ``p_r * bm + i`` for the
   output transform (bit for bit, with the bias);
 * the leaf GEMM's sampled rows against an FP64 product of the same planes
-  within one FP16 ulp plus the FP32 accumulation bound;
+  within one ulp of the plane format plus the FP32 accumulation bound;
 * the whole call through the plan API, dynamic and prepacked, equals the
   staged launches bit for bit.
 
+Every configuration runs with FP16 planes; c4 (rank 49) also runs with the
+BF16 planes of the reference's ``(bfloat16, bfloat16)`` precision pair.
 Sampled block rows always include the first and the last (padded) one.  The
 rank-343 FP16 square product is checked the same way at 16384^3, its
 tensor-core reconstruct within one FP16 ulp plus the FP32 accumulation bound
@@ -64,10 +66,29 @@ def _block_rows(X: torch.Tensor, s: int, pitch: int, index: int) -> torch.Tensor
     return out
 
 
-@pytest.mark.parametrize("config", list(CONFIGS))
-def test_full_size_stages_match_oracle_on_sampled_positions(config):
+# (config, planes): every configuration with FP16 planes, and c4 (rank 49)
+# with the BF16 planes of the reference's (bfloat16, bfloat16) precision pair
+CASES = [(config, "fp16") for config in CONFIGS] + [("c4", "bf16")]
+PLANE_DTYPES = {"fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+def _plane_bits(ref: np.ndarray, planes: str) -> np.ndarray:
+    """Oracle planes (float16, or float32 holding BF16) -> int16 bit patterns."""
+    return ref.view(np.int16) if planes == "fp16" else oracle.bf16_bits(ref).view(np.int16)
+
+
+def _host_products(P: torch.Tensor) -> np.ndarray:
+    """Device products -> the oracle's product input (float16, or float32
+    holding the BF16 values)."""
+    P = P.cpu()
+    return P.numpy() if P.dtype == torch.float16 else P.float().numpy()
+
+
+@pytest.mark.parametrize("config,planes", CASES, ids=lambda v: v)
+def test_full_size_stages_match_oracle_on_sampled_positions(config, planes):
     name, M, K, N, with_bias = CONFIGS[config]
     plan_type = PLANS[name]
+    pd = PLANE_DTYPES[planes]
     s_ = plan_type.scheme_size
     A, W, bias = make_linear_inputs(M, K, N, seed=0, bias=with_bias)
     shape = MatrixShape.from_dimensions(M, K, N, s_)
@@ -76,9 +97,9 @@ def test_full_size_stages_match_oracle_on_sampled_positions(config):
     dev = torch.device("cuda")
     Ad, Wd = A.to(dev), W.to(dev)
     bd = bias.to(dev) if with_bias else None
-    L = torch.empty((R, bm, shape.inner_pitch), device=dev, dtype=torch.float16)
-    Rt = torch.empty((R, bn, shape.inner_pitch), device=dev, dtype=torch.float16)
-    P = torch.empty((R, bm, shape.column_pitch), device=dev, dtype=torch.float16)
+    L = torch.empty((R, bm, shape.inner_pitch), device=dev, dtype=pd)
+    Rt = torch.empty((R, bn, shape.inner_pitch), device=dev, dtype=pd)
+    P = torch.empty((R, bm, shape.column_pitch), device=dev, dtype=pd)
     C = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
     _native.transform_a(name, Ad, L)
     _native.transform_w(name, Wd, Rt)
@@ -88,35 +109,27 @@ def test_full_size_stages_match_oracle_on_sampled_positions(config):
 
     # left and weight transforms, bit for bit
     for i in _sample(bm, 6, seed=1):
-        ref = oracle.left_transform(name, f32(_block_rows(A, s_, bm, i)))  # [R, 1, bk]
-        np.testing.assert_array_equal(_bits(L[:, i, :bk]), ref[:, 0, :].view(np.int16))
+        ref = oracle.left_transform(name, f32(_block_rows(A, s_, bm, i)), planes)  # [R, 1, bk]
+        np.testing.assert_array_equal(_bits(L[:, i, :bk]), _plane_bits(ref[:, 0, :], planes))
     for j in _sample(bn, 6, seed=2):
-        ref = oracle.weight_transform(name, f32(_block_rows(W, s_, bn, j)))  # [R, bk, 1]
-        np.testing.assert_array_equal(_bits(Rt[:, j, :bk]), ref[:, :, 0].view(np.int16))
+        ref = oracle.weight_transform(name, f32(_block_rows(W, s_, bn, j)), planes)  # [R, bk, 1]
+        np.testing.assert_array_equal(_bits(Rt[:, j, :bk]), _plane_bits(ref[:, :, 0], planes))
 
-    # leaf products within the FP16 rounding + FP32 accumulation bound
-    # (FP64 on the device: IEEE double products of the same FP16 planes)
-    Rt64 = Rt[:, :, :bk].double()
-    for i in _sample(bm, 4, seed=3):
-        a = L[:, i, :bk].double()  # [R, bk]
-        exact = torch.einsum("rk,rnk->rn", a, Rt64)
-        magnitude = torch.einsum("rk,rnk->rn", a.abs(), Rt64.abs())
-        got = P[:, i, :bn].double()
-        ulp = torch.clamp(exact.abs(), min=2.0**-14) * 2.0**-10
-        assert torch.all((got - exact).abs() <= ulp + (bk + 2) * 2.0**-23 * magnitude)
-    del Rt64
+    # leaf products within the plane format's rounding + FP32 accumulation
+    # bound (FP64 on the device: IEEE double products of the same planes)
+    _leaf_rows_within_bound(L, Rt, P, _sample(bm, 4, seed=3), bk, bn)
 
     # output transform of the GPU's own products, bit for bit, bias included
     for i in _sample(bm, 6, seed=4):
         rows = [p * bm + i for p in range(s_) if p * bm + i < M]
-        products = P[:, i:i + 1, :bn].cpu().numpy()
+        products = _host_products(P[:, i:i + 1, :bn])
         ref = oracle.output_transform(name, products, len(rows), N, f32(bias) if with_bias else None)
         np.testing.assert_array_equal(_bits(C[rows]), oracle.bf16_bits(ref).view(np.int16))
     assert torch.isfinite(C.float()).all()
 
     # the plan API (dynamic: paired input transforms; prepacked: packed weight)
     # gives the same bits as the staged launches
-    plan = plan_type(M, K, N, dev, dtype=torch.bfloat16, compute_dtype=torch.float16)
+    plan = plan_type(M, K, N, dev, dtype=torch.bfloat16, compute_dtype=pd)
     del L, Rt, P
     ws = plan.allocate_workspace(max_free_memory_fraction=0.9)
     dynamic = plan.run_linear(Ad, Wd, ws, bd)
@@ -129,14 +142,18 @@ def test_full_size_stages_match_oracle_on_sampled_positions(config):
 
 
 def _leaf_rows_within_bound(L, Rt, P, rows, bk, bn):
-    """Sampled product rows against a device-FP64 product of the same planes."""
+    """Sampled product rows against a device-FP64 product of the same planes:
+    one ulp of the plane format (FP16: 11 significand bits; BF16: 8, doubled
+    for slack as half an ulp would do) plus the worst-case FP32 accumulation
+    over ``bk`` terms."""
+    ulp_scale, tiny = (2.0**-10, 2.0**-14) if P.dtype == torch.float16 else (2.0**-7, 2.0**-126)
     Rt64 = Rt[:, :, :bk].double()
     for i in rows:
         a = L[:, i, :bk].double()
         exact = torch.einsum("rk,rnk->rn", a, Rt64)
         magnitude = torch.einsum("rk,rnk->rn", a.abs(), Rt64.abs())
         got = P[:, i, :bn].double()
-        ulp = torch.clamp(exact.abs(), min=2.0**-14) * 2.0**-10
+        ulp = torch.clamp(exact.abs(), min=tiny) * ulp_scale
         assert torch.all((got - exact).abs() <= ulp + (bk + 2) * 2.0**-23 * magnitude)
 
 
