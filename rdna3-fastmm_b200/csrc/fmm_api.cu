@@ -516,6 +516,10 @@ using PairCfg256K128 = LeafGemmPairConfig<256, 3, 128>;
 // epilogue's 16 KiB of shared-memory store buffers)
 using PairCfg256Tma = LeafGemmPairConfig<256, 6, 64, true>;
 using PairCfg256K128Tma = LeafGemmPairConfig<256, 3, 128, true>;
+// narrower pair tiles with 128-deep k-blocks (TMA-store epilogue only): 3
+// stages of 56 KiB at BN = 192, 4 of 48 KiB at BN = 128
+using PairCfg192K128Tma = LeafGemmPairConfig<192, 3, 128, true>;
+using PairCfg128K128Tma = LeafGemmPairConfig<128, 4, 128, true>;
 
 enum GemmVariant {
   kVariantSingle = 0,
@@ -523,7 +527,13 @@ enum GemmVariant {
   kVariantPair128 = 2,
   kVariantPair192 = 3,
   kVariantPair256K128 = 4,  // 256x256 pair tile, 128-deep k-blocks in 3 stages
+  kVariantPair192K128 = 5,  // 256x192 pair tile, 128-deep k-blocks in 3 stages
+  kVariantPair128K128 = 6,  // 256x128 pair tile, 128-deep k-blocks in 4 stages
 };
+
+bool deep_k_variant(int variant) {
+  return variant == kVariantPair256K128 || variant == kVariantPair192K128 || variant == kVariantPair128K128;
+}
 
 // Estimated relative cost of a variant: whole waves of full-tile equivalents
 // over the SMs (or SM pairs), times the padded work one SM does per tile,
@@ -557,6 +567,8 @@ int choose_variant(int64_t rank, int64_t bm, int64_t bn, int sms) {
     if (v == "pair192") return kVariantPair192;
     if (v == "pair128") return kVariantPair128;
     if (v == "pair256k128") return kVariantPair256K128;
+    if (v == "pair192k128") return kVariantPair192K128;
+    if (v == "pair128k128") return kVariantPair128K128;
   }
   int best = kVariantSingle;
   double best_cost = variant_cost(kVariantSingle, rank, bm, bn, sms);
@@ -580,7 +592,7 @@ bool tma_store_epilogue(int variant) {
     if (std::string(v) == "tma") return true;
     if (std::string(v) == "rows") return false;
   }
-  return variant == kVariantPair256K128;
+  return deep_k_variant(variant);
 }
 
 template <class Kernel>
@@ -830,6 +842,9 @@ int launch_leaf_band(int variant, bool tma_store, int rank, const uint16_t* L, c
     return tma_store ? launch_pair<PairCfg256K128Tma, kBf16>(band_l, Rt, prm, ldk, sms, stream)
                      : launch_pair<PairCfg256K128, kBf16>(band_l, Rt, prm, ldk, sms, stream);
   }
+  // the narrow 128-deep configurations exist with the TMA-store epilogue only
+  if (variant == kVariantPair192K128) return launch_pair<PairCfg192K128Tma, kBf16>(band_l, Rt, prm, ldk, sms, stream);
+  if (variant == kVariantPair128K128) return launch_pair<PairCfg128K128Tma, kBf16>(band_l, Rt, prm, ldk, sms, stream);
   if constexpr (!kBf16) {
     if (variant == kVariantPair192) return launch_pair<PairCfg192, false>(band_l, Rt, prm, ldk, sms, stream);
     if (variant == kVariantPair128) return launch_pair<PairCfg128, false>(band_l, Rt, prm, ldk, sms, stream);
@@ -853,9 +868,8 @@ int64_t split_tail_rows(int variant, int64_t bm) {
 }
 
 // FP16 planes (kBf16 = false) or BF16 planes.  The BF16 form carries the
-// 1-SM and the 256 x 256 pair configurations (the ones the cost model picks
-// for every measured shape); a forced narrower pair variant runs as the
-// 256 x 256 pair there.
+// 1-SM configuration and every 128-deep pair configuration; a forced narrower
+// 64-deep pair variant runs as the 256 x 256 pair there.
 template <bool kBf16>
 int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_t bn, int64_t bk,
                      void* P, cudaStream_t stream) {
@@ -869,16 +883,19 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
     return fail(FMM_ERR_TOO_LARGE, "too many GEMM tiles");
   const int sms = usable_sms(info);
   int variant = choose_variant(rank, bm, bn, sms);
-  if (kBf16 && (variant == kVariantPair192 || variant == kVariantPair128)) variant = kVariantPair256;
-  // 128-deep k-blocks in 3 stages with the TMA-store epilogue, from bk = 1024
-  // up (at most 6 % of the last k-block's MMA work is zero padding there):
-  // measured against 64-deep k-blocks in 7 stages with row stores (GEMM alone,
-  // full clock, L2 flushed, 3 interleaved rounds): c2 0.256 -> 0.240 ms, c5a
+  // 128-deep k-blocks with the TMA-store epilogue, from bk = 1024 up (at most
+  // 6 % of the last k-block's MMA work is zero padding there): measured
+  // against 64-deep k-blocks in 7 stages with row stores (GEMM alone, full
+  // clock, L2 flushed, 3 interleaved rounds): c2 0.256 -> 0.240 ms, c5a
   // 0.594 -> 0.557, c5b 4.11-4.17 -> 3.95-4.09 (against 64-deep k-blocks with
-  // the TMA stores there, the previous choice)
-  // (a forced FMM_LEAF_GEMM_VARIANT=pair256 keeps 64-deep k-blocks)
-  if (variant == kVariantPair256 && bk >= 1024 && std::getenv("FMM_LEAF_GEMM_VARIANT") == nullptr)
-    variant = kVariantPair256K128;
+  // the TMA stores there, the previous choice).  A forced
+  // FMM_LEAF_GEMM_VARIANT keeps its own k-depth.
+  if (bk >= 1024 && std::getenv("FMM_LEAF_GEMM_VARIANT") == nullptr) {
+    if (variant == kVariantPair256) variant = kVariantPair256K128;
+    if (variant == kVariantPair192) variant = kVariantPair192K128;
+    if (variant == kVariantPair128) variant = kVariantPair128K128;
+  }
+  if (kBf16 && (variant == kVariantPair192 || variant == kVariantPair128)) variant = kVariantPair256;
   const bool tma_store = tma_store_epilogue(variant);
   const uint16_t* l16 = static_cast<const uint16_t*>(L);
   uint16_t* p16 = static_cast<uint16_t*>(P);

@@ -91,7 +91,8 @@ def test_bf16_reconstruct_matches_oracle_bitwise(shape, with_bias, variant, monk
     np.testing.assert_array_equal(_bits(C), _oracle_bits(ref))
 
 
-@pytest.mark.parametrize("variant", ["single", "pair256", "pair256k128", "pair256-tma", "pair256k128-tma"])
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair256k128", "pair256-tma", "pair256k128-tma",
+                                     "pair192k128-tma", "pair128k128-tma"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
     [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (49, 64, 72, 130), (5, 700, 900, 520)],

@@ -140,7 +140,7 @@ def test_reconstruct_unaligned_bias_matches_aligned(name, variant, monkeypatch):
 
 
 @pytest.mark.parametrize("variant", ["single", "pair256", "pair192", "pair128", "pair256k128",
-                                     "pair256-tma", "pair256k128-tma"])
+                                     "pair256-tma", "pair256k128-tma", "pair192k128-tma", "pair128k128-tma"])
 @pytest.mark.parametrize(
     "rank,bm,bn,bk",
     [(1, 128, 256, 64), (7, 65, 68, 66), (3, 300, 600, 200), (2, 129, 257, 1000), (48, 64, 72, 130),
@@ -148,8 +148,9 @@ def test_reconstruct_unaligned_bias_matches_aligned(name, variant, monkeypatch):
 )
 def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch):
     """Every leaf-GEMM kernel (1-SM 128x256; 2-SM 256x256, 256x192, 256x128 with 64-deep
-    k-blocks; 2-SM 256x256 with 128-deep k-blocks), the 256x256 pairs with both
-    epilogues (per-lane row stores; shared-memory staged TMA stores)."""
+    k-blocks; 2-SM 256x256, 256x192, 256x128 with 128-deep k-blocks), the 256x256
+    pairs with both epilogues (per-lane row stores; shared-memory staged TMA
+    stores), the narrower 128-deep pairs with the TMA stores they carry."""
     variant, _, epilogue = variant.partition("-")
     monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
     monkeypatch.setenv("FMM_LEAF_GEMM_EPILOGUE", epilogue or "rows")
@@ -182,7 +183,7 @@ def test_leaf_gemm_matches_fp64_products(rank, bm, bn, bk, variant, monkeypatch)
     assert torch.all((got - exact).abs() <= bound)
 
 
-@pytest.mark.parametrize("variant", ["single", "pair256", "pair256k128"])
+@pytest.mark.parametrize("variant", ["single", "pair256", "pair256k128", "pair192k128", "pair128k128"])
 def test_leaf_gemm_tile_order_does_not_change_products(variant, monkeypatch):
     """Group sizes and the serpentine N order only reorder whole tiles: the
     products are bitwise those of the default order."""
