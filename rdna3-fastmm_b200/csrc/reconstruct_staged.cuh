@@ -120,10 +120,27 @@ __global__ void __launch_bounds__(StagedReconstructConfig<Prog, STAGES, TP>::kTh
       const bool ready = mbar_wait_bounded(full_bar + 8 * stage, phase, abort, p.timeout_ns, 22);
       if (!__all_sync(0xffffffffu, ready)) break;
       const uint16_t* tile = tiles + size_t(stage) * Cfg::kR * Cfg::kTP;
-      if (j < p.bn) {
-        auto in = [&](int r) -> VecF<2> {
-          return unpack_plane<kBfPlanes, 2>(*reinterpret_cast<const unsigned*>(tile + r * Cfg::kTP + pos));
+      auto in = [&](int r) -> VecF<2> {
+        return unpack_plane<kBfPlanes, 2>(*reinterpret_cast<const unsigned*>(tile + r * Cfg::kTP + pos));
+      };
+      // Interior tile (the same for every thread of the CTA): row i of every
+      // block row lies inside C, every column block's span of the tile lies
+      // inside C, 4-byte stores, no bias.  Each output is then one store
+      // through one of S row pointers at a fixed column offset, without the
+      // per-output bounds and alignment checks of the general path (same
+      // values, same rounding).
+      const int64_t j0 = j - pos;
+      const bool interior = (p.vector_flags & 1) && p.bias == nullptr && i + (S - 1) * p.bm < p.M &&
+                            (S - 1) * p.bn + j0 + Cfg::kTP <= p.N;
+      if (interior) {
+        uint16_t* rowp[S];
+#pragma unroll
+        for (int br = 0; br < S; ++br) rowp[br] = p.C + (br * p.bm + i) * p.ldc + j;
+        auto out = [&](int o, const VecF<2>& x) {
+          store_out_vec<kHalfOut, 2>(rowp[o / S] + (o % S) * p.bn, x);
         };
+        Prog::template run<VecF<2>>(in, out);
+      } else if (j < p.bn) {
         auto out = [&](int o, const VecF<2>& x) {
           store_output_vector<S, 2, kHalfOut>(o, x, i, j, p.bm, p.bn, p.bias, p.C, p.M, p.N, p.ldc,
                                               p.vector_flags);
