@@ -155,8 +155,13 @@ int fmm_reconstruct(int scheme, int dtype, const void* P, int64_t M, int64_t N, 
  * pointers reached over NVLink), each pointing at this rank's first row of
  * the gathered [rows, N] output, with leading dimension `ldc`.  The stores
  * end with a system-scope fence; the caller signals peers (a barrier on the
- * same stream) before they read.  Circuit schemes only (7, 48, 49); rank 343
- * returns FMM_ERR_UNSUPPORTED.  No reference counterpart: the reference is
+ * same stream) before they read.  Rank 48/49 with bn, N and ldc multiples of 8
+ * and 16-byte-aligned destinations run 512-position tiles staged in shared
+ * memory, whose row segments go to every destination as bulk async copies
+ * (one CTA per SM; the grid is the fmm_set_sm_budget budget, so a GEMM
+ * launched beside it with the complementary budget keeps its SMs); other
+ * cases store element vectors from registers.  Circuit schemes only (7, 48,
+ * 49); rank 343 returns FMM_ERR_UNSUPPORTED.  No reference counterpart: the reference is
  * single-GPU; this replaces the reconstruct + NCCL all-gather pair of the
  * multi-GPU form (rdna3_fastmm/distributed.py). */
 int fmm_reconstruct_gather(int scheme, int dtype, const void* P, int64_t M, int64_t N,

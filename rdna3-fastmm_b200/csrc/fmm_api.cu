@@ -281,6 +281,11 @@ template <int SCHEME, int PREC>
 int launch_reconstruct_staged(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
                               void* C, int64_t ldc, DeviceInfo* info, cudaStream_t stream);
 
+template <int SCHEME, int PREC>
+int launch_reconstruct_staged_gather(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
+                                     const GatherDests& dests, int64_t ldc, DeviceInfo* info,
+                                     cudaStream_t stream);
+
 // FMM_RECONSTRUCT_VARIANT=register keeps the circuit schemes on the register
 // reconstruct (the TMA-staged one is the default where a scheme has stages).
 bool staged_reconstruct_enabled() {
@@ -329,6 +334,15 @@ int launch_reconstruct_gather(const void* P, const fmm_dims& d, int64_t M, int64
     constexpr int V = T::kOutVec;
     DeviceInfo* info = nullptr;
     if (int rc = device_info(&info)) return rc;
+    if constexpr (T::kOutStages > 0) {
+      // staged tiles with bulk-copy stores: every output row segment starts on
+      // a 16-byte boundary and moves a multiple of 16 bytes
+      bool bulk = staged_reconstruct_enabled() && aligned(P, 16) && d.ldp % 8 == 0 && d.bn % 8 == 0 &&
+                  N % 8 == 0 && ldc % 8 == 0;
+      for (int k = 0; k < dests.n; ++k) bulk = bulk && aligned(dests.p[k], 16);
+      if (bulk)
+        return launch_reconstruct_staged_gather<SCHEME, PREC>(P, d, M, N, bias, dests, ldc, info, stream);
+    }
     bool vec = (d.bn % V == 0) && (ldc % V == 0);
     for (int k = 0; k < dests.n; ++k) vec = vec && aligned(dests.p[k], 2 * V);
     const bool vec_bias = (d.bn % V == 0) && bias != nullptr && aligned(bias, 2 * V);
@@ -765,6 +779,59 @@ int launch_reconstruct_staged(const void* P, const fmm_dims& d, int64_t M, int64
   kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(map_p, prm);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "staged reconstruct launch");
+  return FMM_OK;
+}
+
+// The staged reconstruct fused with the gather (bulk-copy stores into every
+// destination): 512-position tiles (two TMA boxes) in 3 stages, 8 compute
+// warps, one CTA per SM, the grid the SM budget in force (fmm_set_sm_budget),
+// so a leaf GEMM launched beside it with the complementary budget keeps its
+// SMs whole.
+constexpr int kGatherStages = 3;
+
+template <int SCHEME, int PREC>
+int launch_reconstruct_staged_gather(const void* P, const fmm_dims& d, int64_t M, int64_t N, const void* bias,
+                                     const GatherDests& dests, int64_t ldc, DeviceInfo* info,
+                                     cudaStream_t stream) {
+  using T = SchemeTraits<SCHEME>;
+  using Prog = typename T::Output;
+  using Cfg = StagedGatherConfig<Prog, kGatherStages>;
+  using G = Cfg;
+  auto kernel = reconstruct_staged_gather_kernel<Prog, T::S, kGatherStages, Precision<PREC>::kHalf, Cfg::kTP,
+                                                 Precision<PREC>::kBfPlanes>;
+  static bool configured[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
+  {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (int rc = ensure_smem_attribute(configured[dev], kernel, G::kSmemBytes)) return rc;
+  }
+  CUtensorMap map_p;
+  if (int rc = tiled_map_3d(&map_p, P, {d.ldp, d.bm, int64_t(Cfg::kR)}, {d.ldp * 2, d.bm * d.ldp * 2},
+                            {uint32_t(Cfg::kBoxTP), 1u, uint32_t(Cfg::kR)}, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  StagedReconstructParams prm;
+  prm.bm = d.bm;
+  prm.bn = d.bn;
+  prm.M = M;
+  prm.N = N;
+  prm.ldc = ldc;
+  const int64_t per_row = ceil_div(d.bn, Cfg::kTP);
+  if (d.bm * per_row > 0x7fffffff) return fail(FMM_ERR_TOO_LARGE, "too many reconstruct tiles");
+  prm.tiles_per_row = static_cast<int32_t>(per_row);
+  prm.total_tiles = static_cast<int32_t>(d.bm * per_row);
+  const bool vec_bias = (d.bn % Cfg::kVec == 0) && bias != nullptr && aligned(bias, 2 * Cfg::kVec);
+  prm.vector_flags = vec_bias ? 2 : 0;  // bit 0 (vector stores into C) is unused: copies write C
+  prm.bias = static_cast<const uint16_t*>(bias);
+  prm.C = nullptr;
+  prm.timeout_ns = g_timeout_ns;
+  const int64_t cap = usable_sms(info);
+  const int grid = static_cast<int>(prm.total_tiles < cap ? prm.total_tiles : cap);
+  kernel<<<grid, Cfg::kThreads, G::kSmemBytes, stream>>>(map_p, prm, dests);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "staged gathering reconstruct launch");
   return FMM_OK;
 }
 

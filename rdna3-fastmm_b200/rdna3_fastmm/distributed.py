@@ -167,10 +167,10 @@ class RowShardedLinear:
         row_bytes = self.columns * 2
         done: list = [None] * len(self._products)
         # with chunks the GEMM of chunk c + 1 leaves `reserve_sms` SMs to the
-        # gathering reconstruct of chunk c, which runs beside it
+        # gathering reconstruct of chunk c, which runs beside it on those SMs
         budget = self._reserve() if self.chunks > 1 else False
         try:
-            self._p2p_chunks(local_rows, main, row_bytes, done)
+            self._p2p_chunks(local_rows, main, row_bytes, done, budget)
         finally:
             self._release(budget)
         main.wait_stream(self._side)
@@ -180,7 +180,7 @@ class RowShardedLinear:
         dist.all_reduce(self._flag, group=self.group)
         return self._gather_out
 
-    def _p2p_chunks(self, local_rows: torch.Tensor, main, row_bytes: int, done: list) -> None:
+    def _p2p_chunks(self, local_rows: torch.Tensor, main, row_bytes: int, done: list, reserved: bool) -> None:
         from . import _native
 
         plan, ws = self.plan, self.workspace
@@ -199,8 +199,15 @@ class RowShardedLinear:
             self._side.wait_event(ready)
             with torch.cuda.stream(self._side):
                 dests = [base + start * row_bytes for base in self._peer_bases]
+                if reserved:
+                    # the budget is read when a launch is queued: the gather
+                    # takes the reserved SMs (one CTA each), the next chunk's
+                    # transform and GEMM the rest
+                    _native.set_sm_budget(self.reserve_sms)
                 _native.reconstruct_gather(plan.scheme, P, count, self.columns, self.bias, dests,
                                            self.columns, torch.bfloat16)
+                if reserved:
+                    self._reserve()
             done[k] = torch.cuda.Event()
             done[k].record(self._side)
 

@@ -72,7 +72,8 @@ def test_bf16_transforms_match_oracle_bitwise(shape):
 
 
 @pytest.mark.parametrize("variant", ["staged", "register"])
-@pytest.mark.parametrize("shape", SHAPES + [(2052, 64, 4100)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("shape", SHAPES + [(2052, 64, 4100), (1029, 64, 2064)],
+                         ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_bf16_reconstruct_matches_oracle_bitwise(shape, with_bias, variant, monkeypatch):
     monkeypatch.setenv("FMM_RECONSTRUCT_VARIANT", variant)

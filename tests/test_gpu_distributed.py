@@ -37,13 +37,14 @@ def _worker(rank: int, world: int, port: int, case: tuple, results) -> None:
                             timeout=datetime.timedelta(seconds=60), device_id=device)
     p2p = ce = None
     try:
-        scheme, M, K, N, chunks, with_bias = case
+        scheme, M, K, N, chunks, with_bias, *more = case
+        reserve = more[0] if more else 0
         plan_type = {"rank7": Rank7Plan, "rank48": Rank48Plan}[scheme]
         A, W, bias = make_linear_inputs(M, K, N, seed=0, bias=with_bias)
         A, W = A.to(device), W.to(device)
         bias = bias.to(device) if bias is not None else None
         nccl = RowShardedLinear(plan_type, M, W, bias=bias, chunks=chunks)
-        p2p = RowShardedLinear(plan_type, M, W, bias=bias, chunks=chunks, transport="p2p")
+        p2p = RowShardedLinear(plan_type, M, W, bias=bias, chunks=chunks, transport="p2p", reserve_sms=reserve)
         ce = RowShardedLinear(plan_type, M, W, bias=bias, chunks=chunks, transport="ce")
         rows = nccl.local_rows(A)
         expected = nccl(rows)[:M].clone()
@@ -74,6 +75,9 @@ def _worker(rank: int, world: int, port: int, case: tuple, results) -> None:
     ("rank48", 1024, 512, 768, 1, False),
     ("rank48", 1024, 512, 768, 2, True),
     ("rank7", 1030, 384, 520, 1, True),
+    # chunks with SMs reserved: each chunk's gather runs on the reserved SMs
+    # beside the next chunk's GEMM on the others
+    ("rank48", 4096, 512, 1536, 4, True, 32),
 ], ids=lambda c: "-".join(map(str, c)))
 def test_p2p_gather_matches_nccl_gather(case):
     with mp.Manager() as manager:

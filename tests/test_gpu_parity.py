@@ -92,13 +92,17 @@ def test_weight_transform_handles_full_size_rows():
 # The circuit schemes have two reconstruct kernels: the register one and the
 # TMA-staged persistent one (rank 48/49 default); both must give the oracle's
 # bits.  (2052, 64, 4100) gives ragged 256-position tiles and several tiles a
-# CTA, so the staged pipeline wraps its stages.
+# CTA, so the staged pipeline wraps its stages.  (1029, 64, 2064) allows
+# vector stores, so interior tiles and vectors take the per-tile store path
+# while the last block row (and, for the 256-position tiles, the last column
+# tile) takes the general one.
 RECONSTRUCT_VARIANTS = ["staged", "register"]
+RECONSTRUCT_SHAPES = SHAPES + [(2052, 64, 4100), (1029, 64, 2064)]
 
 
 @pytest.mark.parametrize("variant", RECONSTRUCT_VARIANTS)
 @pytest.mark.parametrize("name", list(PLANS))
-@pytest.mark.parametrize("shape", SHAPES + [(2052, 64, 4100)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("shape", RECONSTRUCT_SHAPES, ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_reconstruct_matches_oracle_bitwise(name, shape, with_bias, variant, monkeypatch):
     monkeypatch.setenv("FMM_RECONSTRUCT_VARIANT", variant)
