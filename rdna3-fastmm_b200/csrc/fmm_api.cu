@@ -634,6 +634,12 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   if (int rc = plane_map(&map_r16, Rt, prm.bk, prm.bn, ldk, prm.rank, 16, prm.bn)) return rc;
   // P[rank][bm][ldp] for the TMA-store epilogue: boxes of 32 columns x 32 rows,
   // 64-byte swizzle (unused by the row-store epilogue)
+  // 16-row boxes of L for the transposed tail tiles' B operand (rows past bm
+  // read as zeros)
+  CUtensorMap map_l16 = map_l;
+  if (prm.tail_rows > 0) {
+    if (int rc = plane_map(&map_l16, L, prm.bk, prm.bm, ldk, prm.rank, 16, prm.plane_rows)) return rc;
+  }
   CUtensorMap map_p = map_l;
   if constexpr (Cfg::kTmaStore) {
     if (int rc = tiled_map_3d(&map_p, prm.P, {prm.ldp, prm.bm, int64_t(prm.rank)},
@@ -646,7 +652,8 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
     if (int rc = ensure_smem_attribute(configured[dev], leaf_gemm_pair_kernel<Cfg, kBf16>, Cfg::kSmemBytes))
       return rc;
   }
-  const int64_t tiles = int64_t(prm.rank) * ceil_div(prm.bm, Cfg::kTileM) * ceil_div(prm.bn, Cfg::kBN);
+  const int64_t tiles =
+      int64_t(prm.rank) * (ceil_div(prm.bm - prm.tail_rows, Cfg::kTileM) * ceil_div(prm.bn, Cfg::kBN) + prm.tail_tiles);
   const int64_t pairs = tiles < sms / 2 ? tiles : sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
@@ -660,7 +667,7 @@ int launch_pair(const void* L, const void* Rt, const LeafGemmParams& prm, int64_
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg, kBf16>, map_l, map_r, map_r16, map_p, prm);
+  e = cudaLaunchKernelEx(&cfg, leaf_gemm_pair_kernel<Cfg, kBf16>, map_l, map_r, map_r16, map_p, map_l16, prm);
   if (e != cudaSuccess) return cuda_fail(e, "leaf GEMM (pair) launch");
   return FMM_OK;
 }
@@ -885,7 +892,7 @@ int leaf_serpentine() {
 template <bool kBf16>
 int launch_leaf_band(int variant, bool tma_store, int rank, const uint16_t* L, const void* Rt,
                      int64_t row0, int64_t rows, int64_t plane_rows, int64_t bn, int64_t bk,
-                     uint16_t* P, int sms, cudaStream_t stream) {
+                     uint16_t* P, int sms, cudaStream_t stream, int64_t transposed_tail = 0) {
   const int64_t ldk = round_up(bk, 8), ldp = round_up(bn, 8);
   const uint16_t* band_l = L + row0 * ldk;
   LeafGemmParams prm;
@@ -899,6 +906,8 @@ int launch_leaf_band(int variant, bool tma_store, int rank, const uint16_t* L, c
   prm.tiles_n = static_cast<int32_t>(ceil_div(bn, GemmCfg::kBN));
   prm.group_m = leaf_group_m();
   prm.serpentine = leaf_serpentine();
+  prm.tail_rows = static_cast<int32_t>(transposed_tail);
+  prm.tail_tiles = transposed_tail > 0 ? static_cast<int32_t>(ceil_div(bn, 256)) : 0;
   prm.P = P + row0 * ldp;
   prm.timeout_ns = g_timeout_ns;
   if (variant == kVariantPair256) {
@@ -934,6 +943,20 @@ int64_t split_tail_rows(int variant, int64_t bm) {
   return (v != nullptr && std::string(v) == "1") ? tail : 0;
 }
 
+// Rows of a short last M tile (1..32 rows) that the 256 x 256 pair kernels
+// compute transposed inside the same launch: P^T = Rt * L_tail^T in 256 x 32
+// tiles over bn, an eighth of a regular tile's MMA work, instead of padding
+// the rows to a whole 256-row tile (c4: bm = 2054, 6 rows).
+// FMM_LEAF_GEMM_TAIL=0 pads them as before; =1 selects the 1-SM band above.
+int64_t transposed_tail_rows(int variant, int64_t bm) {
+  if (variant != kVariantPair256 && variant != kVariantPair256K128) return 0;
+  const int64_t tail = bm % 256;
+  if (bm < 256 || tail == 0 || tail > 32) return 0;
+  const char* v = std::getenv("FMM_LEAF_GEMM_TAIL");
+  if (v != nullptr && (std::string(v) == "0" || std::string(v) == "1")) return 0;
+  return tail;
+}
+
 // FP16 planes (kBf16 = false) or BF16 planes.  The BF16 form carries the
 // 1-SM configuration and every 128-deep pair configuration; a forced narrower
 // 64-deep pair variant runs as the 256 x 256 pair there.
@@ -967,8 +990,9 @@ int launch_leaf_gemm(int rank, const void* L, const void* Rt, int64_t bm, int64_
   const uint16_t* l16 = static_cast<const uint16_t*>(L);
   uint16_t* p16 = static_cast<uint16_t*>(P);
   const int64_t tail = split_tail_rows(variant, bm);
+  const int64_t transposed = tail == 0 ? transposed_tail_rows(variant, bm) : 0;
   if (int rc = launch_leaf_band<kBf16>(variant, tma_store, rank, l16, Rt, 0, bm - tail, bm, bn, bk, p16, sms,
-                                       stream))
+                                       stream, transposed))
     return rc;
   if (tail == 0) return FMM_OK;
   // the short last band: same stream, after the 2-SM launch

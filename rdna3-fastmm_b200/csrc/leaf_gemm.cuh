@@ -51,6 +51,10 @@ struct LeafGemmParams {
   int32_t tiles_m, tiles_n;
   int32_t group_m;
   int32_t serpentine;  // odd groups sweep the N-tiles in reverse
+  // 2-SM kernel, 256-column tiles: the last `tail_rows` (1..32) rows of every
+  // plane are computed transposed, P^T = Rt * L_tail^T, in `tail_tiles`
+  // 256-row tiles over bn per batch (0, 0: no transposed tail)
+  int32_t tail_rows, tail_tiles;
   uint16_t* P;  // FP16 (or BF16) products
   uint64_t timeout_ns;
 };
@@ -82,6 +86,26 @@ __device__ __forceinline__ int tile_n_columns(const LeafGemmParams& p, int tn, i
   const int64_t rem = p.bn - static_cast<int64_t>(tn) * tile_n;
   if (rem >= tile_n) return tile_n;
   return static_cast<int>((rem + granule - 1) / granule * granule);
+}
+
+// 2-SM kernel: tile t -> batch r and either a regular tile (tm, tn) of the
+// rows above the transposed tail, or (transposed) tail tile tm over bn.  Each
+// batch runs its regular tiles (leaf_tile_coords' order) and then its tail
+// tiles, which re-read the batch's Rt planes while they are still in L2.
+__device__ __forceinline__ void pair_tile_coords(const LeafGemmParams& p, int t, int& r, int& tm, int& tn,
+                                                 bool& transposed) {
+  const int regular = p.tiles_m * p.tiles_n;
+  const int per_batch = regular + p.tail_tiles;
+  r = t / per_batch;
+  const int local = t - r * per_batch;
+  transposed = local >= regular;
+  if (transposed) {
+    tm = local - regular;
+    tn = 0;
+    return;
+  }
+  int rr;
+  leaf_tile_coords(p, r * regular + local, rr, tm, tn);
 }
 
 template <class Cfg, bool kBf16 = false>
@@ -355,7 +379,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     leaf_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_l,
                           const __grid_constant__ CUtensorMap tmap_r,
                           const __grid_constant__ CUtensorMap tmap_r16,
-                          const __grid_constant__ CUtensorMap tmap_p, const LeafGemmParams p) {
+                          const __grid_constant__ CUtensorMap tmap_p,
+                          const __grid_constant__ CUtensorMap tmap_l16, const LeafGemmParams p) {
   constexpr int BN = Cfg::kBN;
   constexpr int STAGES = Cfg::kStages;
   constexpr int BK = Cfg::kBK;
@@ -397,6 +422,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tmap_r);
     prefetch_tmap(&tmap_r16);
     if constexpr (Cfg::kTmaStore) prefetch_tmap(&tmap_p);
+    if (p.tail_rows > 0) prefetch_tmap(&tmap_l16);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), Cfg::kTmemCols);
@@ -407,12 +433,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int tiles_m = static_cast<int>((p.bm + Cfg::kTileM - 1) / Cfg::kTileM);
+  // Transposed tail (256-column tiles only: its A operand is a 128-row box of
+  // the Rt map): rows [rows_main, bm) of every plane come from tail tiles
+  // P^T = Rt * L_tail^T with M = 256 Rt rows and N = 32 (16 L rows per CTA,
+  // zero-filled past bm); the regular tiles cover rows [0, rows_main).
+  constexpr bool kTailOk = BN == Cfg::kTileM;
+  const int tail_rows = kTailOk ? p.tail_rows : 0;
+  const int64_t rows_main = p.bm - tail_rows;
+  const int tiles_m = static_cast<int>((rows_main + Cfg::kTileM - 1) / Cfg::kTileM);
   const int tiles_n = static_cast<int>((p.bn + BN - 1) / BN);
   LeafGemmParams q = p;
   q.tiles_m = tiles_m;
   q.tiles_n = tiles_n;
-  const int total_tiles = p.rank * tiles_m * tiles_n;
+  q.tail_rows = tail_rows;
+  q.tail_tiles = tail_rows > 0 ? p.tail_tiles : 0;
+  const int total_tiles = p.rank * (tiles_m * tiles_n + q.tail_tiles);
   const int k_blocks = static_cast<int>((p.bk + BK - 1) / BK);
 
   if (warp == 0) {
@@ -424,14 +459,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int issued = 0;
       for (int t = pair; t < total_tiles && ok; t += pairs) {
         int r, tm, tn;
-        leaf_tile_coords(q, t, r, tm, tn);
+        bool tr;
+        pair_tile_coords(q, t, r, tm, tn, tr);
         const int a_row = tm * Cfg::kTileM + static_cast<int>(cta) * kGemmBM;
         // Each CTA supplies half of the N columns the pair's MMA computes.  A
         // ragged last tile loads exactly its half in 16-row boxes: a BN/2-row
-        // box would fetch rows that belong to the other CTA's half.
-        const int n_cols = tile_n_columns(q, tn, BN, 32);
+        // box would fetch rows that belong to the other CTA's half.  A
+        // transposed tail tile takes its A rows from Rt and 16 L tail rows a CTA.
+        const int n_cols = tr ? 32 : tile_n_columns(q, tn, BN, 32);
         const int half = n_cols / 2;
-        const int b_row = tn * BN + static_cast<int>(cta) * half;
+        const int b_row = tr ? static_cast<int>(rows_main) + static_cast<int>(cta) * 16
+                             : tn * BN + static_cast<int>(cta) * half;
         const uint32_t stage_tx = 2u * (Cfg::kABytes + static_cast<uint32_t>(half) * BK * 2u);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait_bounded_cluster(empty_bar + 8 * stage, phase ^ 1u, abort, p.timeout_ns, 11)) {
@@ -443,9 +481,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int at = 0; at < Cfg::kAtoms; ++at) {
             const int k0 = kb * BK + at * Cfg::kAtomK;
-            tma_load_3d_pair(a_base + stage * Cfg::kABytes + at * Cfg::kAAtomBytes, &tmap_l, full_even,
-                             k0, a_row, r);
+            const uint32_t a_dst = a_base + stage * Cfg::kABytes + at * Cfg::kAAtomBytes;
             const uint32_t b_dst = b_base + stage * Cfg::kBBytes + at * Cfg::kBAtomBytes;
+            if (tr) {
+              tma_load_3d_pair(a_dst, &tmap_r, full_even, k0, a_row, r);
+              tma_load_3d_pair(b_dst, &tmap_l16, full_even, k0, b_row, r);
+              continue;
+            }
+            tma_load_3d_pair(a_dst, &tmap_l, full_even, k0, a_row, r);
             if (n_cols == BN) {
               tma_load_3d_pair(b_dst, &tmap_r, full_even, k0, b_row, r);
             } else {
@@ -481,10 +524,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool issued_any = false;
       for (int t = pair; t < total_tiles && ok; t += pairs) {
         int r, tm, tn;
-        leaf_tile_coords(q, t, r, tm, tn);
+        bool tr;
+        pair_tile_coords(q, t, r, tm, tn, tr);
         // M = 256, cta_group::2: N a multiple of 32 (16 columns from each CTA)
-        const uint32_t idesc =
-            idesc_kind_f16<kBf16>(Cfg::kTileM, static_cast<uint32_t>(tile_n_columns(q, tn, BN, 32)));
+        const uint32_t idesc = idesc_kind_f16<kBf16>(
+            Cfg::kTileM, static_cast<uint32_t>(tr ? 32 : tile_n_columns(q, tn, BN, 32)));
         if (!mbar_wait_bounded_cluster(tempty_bar + 8 * acc, acc_phase ^ 1u, abort, p.timeout_ns, 12)) {
           ok = false;
           break;
@@ -539,7 +583,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int chunk = 0;  // kTmaStore: running count of this warp's staged blocks (buffer = chunk & 1)
     for (int t = pair; t < total_tiles; t += pairs) {
       int r, tm, tn;
-      leaf_tile_coords(q, t, r, tm, tn);
+      bool tr;
+      pair_tile_coords(q, t, r, tm, tn, tr);
       int ready = 0;
       if (lane == 0)
         ready = mbar_wait_bounded_cluster(tfull_bar + 8 * acc, acc_phase, abort, p.timeout_ns, 14) ? 1 : 0;
@@ -550,7 +595,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint16_t* prow = p.P + (static_cast<int64_t>(r) * p.plane_rows + row) * p.ldp;
       const uint32_t t_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const int n_cols = tile_n_columns(q, tn, BN, 32);
+      if (tr) {
+        // transposed tail: this lane holds Rt row (P column) col for the 32 L
+        // tail rows (TMEM columns); for each valid tail row the warp writes 32
+        // consecutive columns of P
+        uint32_t v[32];
+        tc_ld_32x32b_x32(t_addr, v);
+        tc_wait_ld();
+        const int64_t col = static_cast<int64_t>(tm) * Cfg::kTileM + row_in_tile;
+        if (col < p.bn) {
+          uint16_t* pc = p.P + (static_cast<int64_t>(r) * p.plane_rows + rows_main) * p.ldp + col;
+#pragma unroll
+          for (int n = 0; n < 32; ++n)
+            if (n < tail_rows)
+              pc[n * p.ldp] = static_cast<uint16_t>(pack2_rn<kBf16>(__uint_as_float(v[n]), 0.0f) & 0xFFFFu);
+        }
+      }
+      const int n_cols = tr ? 0 : tile_n_columns(q, tn, BN, 32);
 #pragma unroll 1
       for (int c = 0; c < n_cols; c += 32) {
         uint32_t v[32];

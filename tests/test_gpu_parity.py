@@ -214,13 +214,16 @@ def test_leaf_gemm_tile_order_does_not_change_products(variant, monkeypatch):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
 @pytest.mark.parametrize("variant", ["pair256", "pair256k128"])
-@pytest.mark.parametrize("rank,bm,bn,bk", [(3, 262, 300, 200), (2, 517, 260, 136), (48, 2054, 72, 64)])
-def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, dtype, monkeypatch):
-    """A short last M band (bm % 256 <= 128) run as a second, 1-SM launch over
-    the planes' last rows (FMM_LEAF_GEMM_TAIL=1 forces the split): the rows of
-    the 2-SM band equal the single-launch products bit for bit, the band's rows
-    stay within the product bound of an FP64 product, and nothing outside the
-    planes is written."""
+@pytest.mark.parametrize("rank,bm,bn,bk", [(3, 262, 300, 200), (2, 517, 260, 136), (48, 2054, 72, 64),
+                                           (2, 288, 520, 300), (3, 273, 700, 1100)])
+def test_leaf_gemm_short_last_tile_modes(rank, bm, bn, bk, variant, dtype, monkeypatch):
+    """A short last M tile (bm % 256 rows) three ways: padded to a whole
+    256-row tile (FMM_LEAF_GEMM_TAIL=0), a second 1-SM launch over the planes'
+    last rows (=1), and, by default for up to 32 rows, 256 x 32 tiles computed
+    transposed (P^T = Rt * L_tail^T) in the same launch.  The rows above the
+    tail equal the padded products bit for bit in every mode, the tail rows stay
+    within the product bound of an FP64 product, and nothing outside the planes
+    is written."""
     monkeypatch.setenv("FMM_LEAF_GEMM_VARIANT", variant)
     g = torch.Generator().manual_seed(bm)
     ldk, ldp = -(-bk // 8) * 8, -(-bn // 8) * 8
@@ -230,8 +233,11 @@ def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, dtype, monk
     Rt[:, :, :bk] = torch.randn((rank, bn, bk), generator=g).to(dtype)
     L, Rt = L.cuda(), Rt.cuda()
     outs = []
-    for tail in ("0", "1"):
-        monkeypatch.setenv("FMM_LEAF_GEMM_TAIL", tail)
+    for tail in ("0", "1", None):
+        if tail is None:
+            monkeypatch.delenv("FMM_LEAF_GEMM_TAIL", raising=False)
+        else:
+            monkeypatch.setenv("FMM_LEAF_GEMM_TAIL", tail)
         P_all = torch.full((rank * bm * ldp + ldp,), float("nan"), device="cuda", dtype=dtype)
         P = P_all[: rank * bm * ldp].view(rank, bm, ldp)
         _native.leaf_gemm(rank, L, Rt, bm, bn, bk, P)
@@ -240,13 +246,15 @@ def test_leaf_gemm_with_a_split_tail_band(rank, bm, bn, bk, variant, dtype, monk
         assert torch.isfinite(P[:, :, :bn]).all()
         outs.append(P[:, :, :bn].clone())
     main = bm - bm % 256
-    assert torch.equal(outs[0][:, :main].view(torch.int16), outs[1][:, :main].view(torch.int16))
     a, b = L[:, main:, :bk].double().cpu(), Rt[:, :, :bk].double().cpu().transpose(1, 2)
     exact = torch.matmul(a, b)
     # one ulp of the product format (10 or 7 significand bits) + FP32 accumulation
     ulp = 2.0**-10 if dtype == torch.float16 else 2.0**-7
     bound = torch.clamp(exact.abs(), min=2.0**-14) * ulp + (bk + 2) * 2.0**-23 * torch.matmul(a.abs(), b.abs())
-    assert torch.all((outs[1][:, main:].cpu().double() - exact).abs() <= bound)
+    for out in outs[1:]:
+        assert torch.equal(outs[0][:, :main].view(torch.int16), out[:, :main].view(torch.int16))
+    for out in outs:
+        assert torch.all((out[:, main:].cpu().double() - exact).abs() <= bound)
 
 
 @pytest.mark.parametrize("name", list(PLANS))
