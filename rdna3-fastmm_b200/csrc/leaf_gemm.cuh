@@ -341,7 +341,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // No TMA multicast is used: every CTA loads only its own halves.  Leaves with
 // bk >= 1024 run 128-deep k-blocks in 3 stages (two 64-deep atom columns per
 // operand and stage, half the barrier round trips per FLOP) with the TMA-store
-// epilogue; the host picks the configuration (fmm_api.cu).
+// epilogue; the host picks the configuration (fmm_api.cu).  With 256-column
+// tiles a short last M tile of 1..32 rows is computed transposed (tail tiles
+// after each batch's regular tiles, pair_tile_coords): A = 128 Rt rows a CTA,
+// B = 16 L tail rows a CTA, N = 32, and the epilogue writes the tail rows of P
+// column by column.
 template <int BN, int STAGES, int BK = kGemmBK, bool TMA_STORE = false>
 struct LeafGemmPairConfig {
   static constexpr int kBN = BN;
