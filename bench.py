@@ -679,6 +679,21 @@ def default_transport(world: int) -> str:
     return "ce" if world == 2 else "p2p"
 
 
+def default_chunking(transport: str, world: int) -> tuple[int, int]:
+    """(row chunks per rank, SMs the GEMM leaves free) per gather transport.
+    NCCL and the copy engines overlap chunk c's gather with chunk c + 1 (NCCL
+    measured best with 32 SMs left to it).  The fused reconstruct from 3 GPUs
+    up runs 4 chunks with 48 SMs reserved: its bulk-copy gather kernel takes
+    exactly the reserved SMs beside the next chunk's GEMM.  In the per-GPU load
+    of the 4- and 8-GPU c5b step, emulated on 2 GPUs, that took 2.825 -> 2.405 ms
+    and 2.575 -> 2.312 ms against one chunk with the register gather kernel
+    (24-32 reserved SMs, or 2 chunks, gained less or lost).  At 2 GPUs the
+    step is compute-bound and p2p keeps one chunk."""
+    if transport == "p2p":
+        return (4, 48) if world >= 3 else (1, 0)
+    return 4, 32
+
+
 def workload_config(args) -> dict:
     """The workload keys both arms report (the same dict for the same flags)."""
     scheme, M, K, N, with_bias, prepacked, description = WORKLOADS[args.workload]
@@ -737,11 +752,12 @@ def main() -> None:
     parser.add_argument("--no-numa-bind", action="store_true",
                         help="leave the e2e pinned buffers wherever the default policy puts them")
     parser.add_argument("--chunks", type=int, default=None,
-                        help="row chunks per rank when sharded (default: 4 with the NCCL gather, "
-                             "which overlaps the next chunk; 1 with --transport p2p)")
-    parser.add_argument("--reserve-sms", type=int, default=32,
+                        help="row chunks per rank when sharded (default: 4, which overlaps each "
+                             "chunk's gather with the next chunk; 1 with --transport p2p on 2 GPUs)")
+    parser.add_argument("--reserve-sms", type=int, default=None,
                         help="SMs the GEMM leaves free, while sharded chunks compute, for the NCCL "
-                             "all-gather or the gathering reconstruct of the previous chunk")
+                             "all-gather or the gathering reconstruct of the previous chunk "
+                             "(default: 48 for p2p, 32 for NCCL)")
     parser.add_argument("--transport", choices=("nccl", "p2p", "ce"), default=None,
                         help="sharded gather: NCCL all-gather, the reconstruct kernel storing "
                              "into every rank's peer-mapped buffer over NVLink (p2p), or copy-engine "
@@ -753,8 +769,11 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.transport is None:
         args.transport = default_transport(int(os.environ.get("WORLD_SIZE", "1")))
+    default_chunks, default_reserve = default_chunking(args.transport, int(os.environ.get("WORLD_SIZE", "1")))
     if args.chunks is None:
-        args.chunks = 1 if args.transport == "p2p" else 4
+        args.chunks = default_chunks
+    if args.reserve_sms is None:
+        args.reserve_sms = default_reserve
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -31,6 +31,15 @@ def test_default_transport_follows_the_measurements():
     assert bench.default_transport(8) == "p2p"
 
 
+def test_default_chunking_follows_the_measurements():
+    bench = _bench()
+    assert bench.default_chunking("p2p", 8) == (4, 48)
+    assert bench.default_chunking("p2p", 4) == (4, 48)
+    assert bench.default_chunking("p2p", 2) == (1, 0)
+    assert bench.default_chunking("nccl", 8) == (4, 32)
+    assert bench.default_chunking("ce", 2) == (4, 32)
+
+
 def test_workload_config_is_the_benchmark_configuration():
     bench = _bench()
     config = bench.workload_config(_args())
