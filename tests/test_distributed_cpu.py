@@ -111,3 +111,50 @@ def test_transport_arguments_are_validated():
         assert layer.transport == "nccl"
     finally:
         dist.destroy_process_group()
+
+
+def test_p2p_chunks_give_the_gather_the_reserved_sms(monkeypatch):
+    """With chunks and reserved SMs, each chunk's transform and GEMM are queued
+    under the budget that leaves `reserve_sms` SMs free, and its gathering
+    reconstruct under a budget of exactly `reserve_sms` (the kernel runs one
+    CTA per SM), so it runs beside the next chunk's GEMM.  The budget is
+    released afterwards.  CUDA streams, events and the library are replaced
+    by recorders: this pins the host-side order only."""
+    import contextlib
+    from types import SimpleNamespace
+
+    from rdna3_fastmm import _native
+
+    log, budget = [], [0]
+    monkeypatch.setattr(_native, "set_sm_budget", lambda n: budget.__setitem__(0, n))
+    monkeypatch.setattr(_native, "transform_a", lambda *a: log.append(("transform", budget[0])))
+    monkeypatch.setattr(_native, "leaf_gemm", lambda *a: log.append(("gemm", budget[0])))
+    monkeypatch.setattr(_native, "reconstruct_gather", lambda *a: log.append(("gather", budget[0])))
+
+    class Event:
+        def record(self, stream=None):
+            pass
+
+    class Stream:
+        def wait_event(self, event):
+            pass
+
+    monkeypatch.setattr(torch.cuda, "Event", Event)
+    monkeypatch.setattr(torch.cuda, "stream", lambda stream: contextlib.nullcontext())
+    monkeypatch.setattr(torch.cuda, "get_device_properties",
+                        lambda device: SimpleNamespace(multi_processor_count=148))
+    layer = object.__new__(RowShardedLinear)
+    layer.plan = SimpleNamespace(scheme="rank48", rank=48,
+                                 shape=SimpleNamespace(block_rows=512, block_columns=3072, block_inner=1152))
+    layer.workspace = SimpleNamespace(left_transformed=None)
+    layer.packed = SimpleNamespace(transformed=None)
+    layer._products = [object(), object()]
+    layer.world, layer.rank, layer.chunks, layer.chunk_rows = 2, 0, 4, 2048
+    layer.reserve_sms, layer.device, layer.columns, layer.bias = 48, "cpu", 12288, None
+    layer._side = Stream()
+    layer._peer_bases = [0, 1 << 40]
+    reserved = layer._reserve()
+    layer._p2p_chunks(torch.zeros((4 * 2048, 8)), Stream(), 12288 * 2, [None, None], reserved)
+    layer._release(reserved)
+    assert log == [("transform", 100), ("gemm", 100), ("gather", 48)] * 4
+    assert budget[0] == 0
