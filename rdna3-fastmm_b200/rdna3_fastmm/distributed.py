@@ -19,12 +19,17 @@ tensor-core work.
 kernel (``fmm_reconstruct_gather``): every rank exports its gather buffer by
 CUDA IPC and maps its peers' buffers (plain peer mappings, no multicast
 object), and each rank's output transform stores every output vector into its
-own buffer and, over NVLink, into every peer's buffer at this rank's rows.  With ``chunks > 1`` the gathering
-reconstruct of chunk c runs on a side stream while chunk c + 1 transforms and
-multiplies (two product workspaces alternate), so NVLink traffic overlaps
-tensor-core work without reserving SMs for a collective.  A one-element
-all-reduce queued behind the kernels makes every peer's rows visible before
-the result is used.
+own buffer and, over NVLink, into every peer's buffer at this rank's rows
+(for rank 48/49 with 16-byte-aligned rows: row segments staged in shared
+memory and written by bulk async copies, one CTA per SM).  With ``chunks > 1``
+the gathering reconstruct of chunk c runs on a side stream while chunk c + 1
+transforms and multiplies (two product workspaces alternate).  With
+``reserve_sms`` as well, the transform and GEMM are queued under an SM budget
+that leaves ``reserve_sms`` SMs free, and the gather under a budget of exactly
+``reserve_sms``, so NVLink traffic overlaps tensor-core work on disjoint SMs
+(from 3 GPUs up, ``chunks=4, reserve_sms=48`` measured best on c5b).  A
+one-element all-reduce queued behind the kernels makes every peer's rows
+visible before the result is used.
 
 ``transport="ce"`` keeps the reconstruct local (each chunk's rows land in this
 rank's own IPC-exported output buffer) and hands the transfer to the copy
