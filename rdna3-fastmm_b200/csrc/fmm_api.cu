@@ -803,7 +803,6 @@ int launch_reconstruct_staged_gather(const void* P, const fmm_dims& d, int64_t M
   using T = SchemeTraits<SCHEME>;
   using Prog = typename T::Output;
   using Cfg = StagedGatherConfig<Prog, kGatherStages>;
-  using G = Cfg;
   auto kernel = reconstruct_staged_gather_kernel<Prog, T::S, kGatherStages, Precision<PREC>::kHalf, Cfg::kTP,
                                                  Precision<PREC>::kBfPlanes>;
   static bool configured[kMaxDevices] = {};
@@ -813,7 +812,7 @@ int launch_reconstruct_staged_gather(const void* P, const fmm_dims& d, int64_t M
   if (dev < 0 || dev >= kMaxDevices) return fail(FMM_ERR_UNSUPPORTED, "device index out of range");
   {
     std::lock_guard<std::mutex> lock(g_device_mutex);
-    if (int rc = ensure_smem_attribute(configured[dev], kernel, G::kSmemBytes)) return rc;
+    if (int rc = ensure_smem_attribute(configured[dev], kernel, Cfg::kSmemBytes)) return rc;
   }
   CUtensorMap map_p;
   if (int rc = tiled_map_3d(&map_p, P, {d.ldp, d.bm, int64_t(Cfg::kR)}, {d.ldp * 2, d.bm * d.ldp * 2},
@@ -836,7 +835,7 @@ int launch_reconstruct_staged_gather(const void* P, const fmm_dims& d, int64_t M
   prm.timeout_ns = g_timeout_ns;
   const int64_t cap = usable_sms(info);
   const int grid = static_cast<int>(prm.total_tiles < cap ? prm.total_tiles : cap);
-  kernel<<<grid, Cfg::kThreads, G::kSmemBytes, stream>>>(map_p, prm, dests);
+  kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(map_p, prm, dests);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "staged gathering reconstruct launch");
   return FMM_OK;

@@ -225,14 +225,13 @@ __global__ void __launch_bounds__(StagedGatherConfig<Prog, STAGES, TP>::kThreads
     reconstruct_staged_gather_kernel(const __grid_constant__ CUtensorMap tmap_p,
                                      const StagedReconstructParams p, const GatherDests dests) {
   using Cfg = StagedGatherConfig<Prog, STAGES, TP>;
-  using G = Cfg;
   constexpr int kOut = Prog::kOutputs;
   constexpr int kComputeThreads = Cfg::kComputeWarps * 32;
   extern __shared__ __align__(128) uint8_t gather_smem[];
   const uint16_t* tiles = reinterpret_cast<const uint16_t*>(gather_smem);
   const uint32_t tiles_base = smem_u32(gather_smem);
   const uint32_t out_base = tiles_base + STAGES * Cfg::kTileBytes;  // [2][kOut][TP] elements
-  uint64_t* bars = reinterpret_cast<uint64_t*>(gather_smem + size_t(STAGES) * Cfg::kTileBytes + 2 * G::kOutBufBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gather_smem + size_t(STAGES) * Cfg::kTileBytes + 2 * Cfg::kOutBufBytes);
   const uint32_t full_bar = smem_u32(bars);
   const uint32_t empty_bar = smem_u32(bars + STAGES);
   volatile int* abort = reinterpret_cast<volatile int*>(bars + 2 * STAGES);
@@ -275,7 +274,7 @@ __global__ void __launch_bounds__(StagedGatherConfig<Prog, STAGES, TP>::kThreads
     // threads leave together if a wait gave up
     bulk_wait_group_read<1>();
     if (!named_barrier_and(1, kComputeThreads, ready)) break;
-    const uint32_t buf = out_base + static_cast<uint32_t>(n & 1) * G::kOutBufBytes;
+    const uint32_t buf = out_base + static_cast<uint32_t>(n & 1) * Cfg::kOutBufBytes;
     if (j < p.bn) {
       // this thread's box and its position inside the box
       const uint16_t* box = tiles + size_t(stage) * Cfg::kTileBytes / 2 +
